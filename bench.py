@@ -1,0 +1,324 @@
+#!/usr/bin/env python3
+"""Benchmark: emulated NVFP4 GEMM MAC/s at M=N=K=8192 on B200 (one process per GPU).
+
+Workload (the configuration the headline metric is quoted on): A, B = |N(0,1)| fp16 [8192, 8192]
+with 1% of the K columns (the same 82 indices in A and B, seeded) scaled by 100 -- seeded synthetic
+data, drawn on the CPU and moved to the GPU.  One step = the public path a caller runs per case:
+``quant_fn(A, B)`` (device global scales + NVFP4 quantisation of both operands) then
+``emul_fn(state)`` (the emulated GEMM, fp16 out as the reference NVFP emulator returns).
+``value`` is M*N*K per step with inputs resident in HBM; ``e2e`` adds the host->device copy of A, B
+from pinned memory and the device->host copy of the output.  Multi-GPU: every rank runs its own
+seeded case (weak scaling); timing is the max over ranks of CUDA-event time.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+if str(REPO) not in sys.path:
+    sys.path.insert(0, str(REPO))
+
+M = N = K = 8192
+OUTLIER_FRAC = 0.01
+SEED = 1234
+CPU_SAMPLE = (1024, 1024, 8192)   # rows of A, rows of B, K for the CPU baseline sample
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def make_inputs(rank: int):
+    import torch
+
+    g = torch.Generator().manual_seed(SEED + rank)
+    a = torch.randn(M, K, generator=g).abs_()
+    b = torch.randn(N, K, generator=g).abs_()
+    cols = torch.randperm(K, generator=g)[: int(round(K * OUTLIER_FRAC))]
+    a[:, cols] *= 100.0
+    b[:, cols] *= 100.0
+    return a.half(), b.half()
+
+
+def peaks():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.is_file():
+        d = json.loads(p.read_text())
+        return d, "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "sm_max_mhz": 1965.0}, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while the timed region runs."""
+
+    FIELDS = "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active"
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = Path(os.environ.get("TMPDIR", "/tmp")) / f"emugen_clocks_{os.getpid()}.csv"
+
+    def __enter__(self):
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-i", str(self.index), "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.f.close()
+
+    def summary(self):
+        REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+                   0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+                   0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting"}
+        try:
+            rows = [r.split(",") for r in self.path.read_text().strip().splitlines() if r.strip()]
+        except Exception:
+            rows = []
+        sm, mx, reasons = [], None, set()
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                mx = float(r[2])
+                bits = int(r[4].strip(), 16)
+                for k, v in REASONS.items():
+                    if bits & k and v != "gpu_idle":
+                        reasons.add(v)
+            except Exception:
+                continue
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def cpu_baseline(state_cpu, steps: int = 1):
+    """Reference C++ emulator (compiled from the reference's own source into oracle/_ref) on the host
+    cores, on a bounded slice of the same quantised workload.  Returns the cpu_baseline object."""
+    import torch
+
+    from oracle import ref as oref
+
+    mod = oref.load("nvfp")
+    if mod is None:
+        return None
+    torch.set_num_threads(os.cpu_count() or 1)
+    ms, ns, ks = CPU_SAMPLE
+    a = state_cpu["a_fp4"][:ms, : ks // 2].contiguous()
+    b = state_cpu["b_fp4"][:ns, : ks // 2].contiguous()
+    sa = state_cpu["scale_a"][: ((ms + 127) // 128) * 128].contiguous()
+    sb = state_cpu["scale_b"][: ((ns + 127) // 128) * 128].contiguous()
+    mod.emulated_scaled_fp4_mm(a[:128], b[:128], sa[:128], sb[:128], state_cpu["alpha"], 128, 0, 0)  # warm
+    times = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        mod.emulated_scaled_fp4_mm(a, b, sa, sb, state_cpu["alpha"], 128, 0, 0)
+        times.append(time.perf_counter() - t0)
+    t = min(times)
+    return {"value": ms * ns * ks / t, "unit": "MAC/s", "cores": torch.get_num_threads(), "kind": "reference",
+            "sample": f"reference nvfp_emulation.cpp emulated_scaled_fp4_mm on CPU tensors, {ms}x{ns}x{ks} slice of "
+                      f"the quantised 8192^3 workload, best of {steps} after a warm call, {t:.2f} s"}
+
+
+def run_reference_arm(args, rank: int, world: int) -> int:
+    """--impl reference: the reference's own CPU emulator, timed on this host's cores."""
+    if rank != 0:
+        return 0
+    import torch
+
+    from oracle import ref as oref
+
+    mod = oref.load("nvfp")
+    cfg = {"workload": "NVFP4 emulated GEMM 8192^3, |N(0,1)| + 1% x100 outlier columns, fp16 out",
+           "sample": "%dx%dx%d slice per step" % CPU_SAMPLE}
+    if mod is None:
+        print(json.dumps({"impl": "reference", "unavailable": "reference C++ emulator not built into oracle/_ref"}))
+        return 0
+    torch.set_num_threads(os.cpu_count() or 1)
+    # quantised state for the slice, produced on the CPU with the oracle-side numpy quantiser (the
+    # reference's own quantiser is GPU-only third-party code); only the emulator is timed
+    import numpy as np
+
+    from tests.golden.make_golden import pad, quant_nvfp4_np, swizzle
+
+    ms, ns, ks = CPU_SAMPLE
+    a16, b16 = make_inputs(0)
+    xa = a16[:ms, :ks].float().numpy()
+    xb = b16[:ns, :ks].float().numpy()
+    ga = np.float32(2688.0 / np.abs(a16.float().numpy()).max())
+    gb = np.float32(2688.0 / np.abs(b16.float().numpy()).max())
+    qa, sa = quant_nvfp4_np(xa, ga)
+    qb, sb = quant_nvfp4_np(xb, gb)
+    G = ks // 16
+    ta, tb = torch.from_numpy(qa), torch.from_numpy(qb)
+    tsa = torch.from_numpy(swizzle(sa, pad(ms, 128), pad(G, 4))).view(torch.float8_e4m3fn)
+    tsb = torch.from_numpy(swizzle(sb, pad(ns, 128), pad(G, 4))).view(torch.float8_e4m3fn)
+    alpha = torch.tensor([1.0 / (float(ga) * float(gb))], dtype=torch.float32)
+    for _ in range(args.warmup):
+        mod.emulated_scaled_fp4_mm(ta[:128], tb[:128], tsa[:128], tsb[:128], alpha, 128, 0, 0)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        mod.emulated_scaled_fp4_mm(ta, tb, tsa, tsb, alpha, 128, 0, 0)
+        times.append(time.perf_counter() - t0)
+    t = sum(times) / len(times)
+    v = ms * ns * ks / t
+    line = {"impl": "reference", "metric": "emulated FP4 GEMM MAC/s at 8192^3", "value": v, "unit": "MAC/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+            "config": cfg,
+            "cpu_baseline": {"value": v, "unit": "MAC/s", "cores": torch.get_num_threads(), "kind": "reference",
+                             "sample": "reference C++ emulator (nvfp_emulation.cpp) on CPU tensors, %dx%dx%d per step"
+                                       % CPU_SAMPLE},
+            "e2e": {"value": v, "unit": "MAC/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line))
+    return 0
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        log("warmup raised to 3 (minimum)")
+        args.warmup = 3
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference_arm(args, rank, world)
+
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+
+    from emugen_b200.backends.nvfp import build_nvfp_fns
+
+    quant_fn, _real_fn, emul_fn, _meta = build_nvfp_fns(out_dtype=torch.bfloat16)
+    a_h, b_h = make_inputs(rank)
+    a_d, b_d = a_h.to(dev), b_h.to(dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step(a, b, ev=None):
+        st = quant_fn(a, b)
+        if ev is not None:
+            ev[0].record(stream)
+        out = emul_fn(st)
+        if ev is not None:
+            ev[1].record(stream)
+        return st, out
+
+    for _ in range(args.warmup):
+        st, out = step(a_d, b_d)
+    torch.cuda.synchronize()
+
+    # ---- timed region: device-resident inputs
+    gemm_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        t0.record(stream)
+        for i in range(args.steps):
+            st, out = step(a_d, b_d, gemm_ev[i])
+        t1.record(stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms_local = t0.elapsed_time(t1)
+    gemm_ms = sum(s.elapsed_time(e) for s, e in gemm_ev) / args.steps
+
+    # ---- end to end: pinned host inputs -> device -> quant + emul -> host output
+    a_p, b_p = a_h.pin_memory(), b_h.pin_memory()
+    out_h = torch.empty((M, N), dtype=torch.float16).pin_memory()
+    for _ in range(2):
+        _, o = step(a_p.to(dev, non_blocking=True), b_p.to(dev, non_blocking=True))
+        out_h.copy_(o, non_blocking=True)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    e0.record(stream)
+    for _ in range(args.steps):
+        _, o = step(a_p.to(dev, non_blocking=True), b_p.to(dev, non_blocking=True))
+        out_h.copy_(o, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_local = e0.elapsed_time(e1)
+
+    times = torch.tensor([ms_local, e2e_local, gemm_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(times, op=dist.ReduceOp.MAX)
+    ms_max, e2e_max, gemm_max = times.tolist()
+
+    if rank == 0:
+        macs = M * N * K
+        value = world * macs * args.steps / (ms_max / 1e3)
+        e2e_v = world * macs * args.steps / (e2e_max / 1e3)
+        pk, pk_kind = peaks()
+        achieved = 2.0 * macs / (gemm_max / 1e3) / 1e12
+        peak = pk.get("bf16_tflops", 1590.0)
+        cpu = None
+        if not args.no_cpu_baseline and world == 1:
+            try:
+                sc = {k: getattr(st, k).detach().cpu() for k in ("a_fp4", "b_fp4", "scale_a", "scale_b", "alpha")}
+                cpu = cpu_baseline(sc)
+            except Exception as e:  # reported, not fatal
+                cpu = {"value": None, "error": f"{type(e).__name__}: {e}"}
+        line = {
+            "metric": "emulated FP4 GEMM MAC/s at 8192^3",
+            "value": value, "unit": "MAC/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int32/f64", "data": "synthetic",
+            "config": {"workload": "NVFP4 emulated GEMM M=N=K=8192 per GPU, fp16 A/B |N(0,1)| with 1% outlier "
+                                   "columns x100, quant_fn + emul_fn per step, fp16 out",
+                       "M": M, "N": N, "K": K, "format": "nvfp4", "w_reduce": 4, "rounding": "RZ/RZ",
+                       "l2": "inputs larger than L2 (fp16 A+B = 268 MB read per step)",
+                       "parallelism": f"independent case per GPU x{world}"},
+            "e2e": {"value": e2e_v, "unit": "MAC/s", "h2d_bytes_per_step": 2 * M * K * 2, "d2h_bytes_per_step": M * N * 2},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak, "traffic": None, "kernel": "emul_gemm",
+                         "kernel_ms": gemm_max, "peak_kind": f"bf16 dense burst ({pk_kind})"},
+            "gpu_launches": 6 * args.steps,
+            "clocks": clk.summary(),
+        }
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line))
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

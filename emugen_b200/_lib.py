@@ -1,0 +1,203 @@
+"""ctypes binding of libemugen.so (include/emugen.h) plus the torch-tensor glue.
+
+The library is the product: every emulated GEMM and quantisation below runs in its CUDA kernels.
+There is no CPU fallback.  If the shared library is missing this module raises at first use
+(build it with ``python -m emugen_b200.build``); CPU tensors are computed on the current CUDA
+device and copied back, and without a CUDA device every call raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+import torch
+
+PKG = Path(__file__).resolve().parent
+LIB_PATH = PKG / "libemugen.so"
+
+# enums of include/emugen.h
+EMU_OK = 0
+EMU_FMT_NVFP4, EMU_FMT_MXFP4 = 0, 1
+EMU_RZ, EMU_RNE = 0, 1
+EMU_OUT_F16, EMU_OUT_BF16_VIA_F16, EMU_OUT_F32 = 0, 1, 2
+EMU_DTYPE_F16, EMU_DTYPE_BF16 = 0, 1
+ABI_VERSION = 1
+
+SYMBOLS = ("emu_abi_version", "emu_last_error", "emu_status_string", "emu_gemm",
+           "emu_nvfp4_global_scales", "emu_quant_nvfp4", "emu_quant_mxfp4")
+
+
+class EmuGemmParams(ctypes.Structure):
+    _fields_ = [("format", ctypes.c_int32), ("group_size", ctypes.c_int32), ("w_reduce", ctypes.c_int32),
+                ("stage3_rounding", ctypes.c_int32), ("stage4_rounding", ctypes.c_int32),
+                ("out_mode", ctypes.c_int32)]
+
+
+class EmuError(RuntimeError):
+    """A failing libemugen call; ``status`` is the emu_status code."""
+
+    def __init__(self, status: int, message: str):
+        super().__init__(message)
+        self.status = status
+
+
+_lib = None
+_lock = threading.Lock()
+
+
+def load() -> ctypes.CDLL:
+    """Load libemugen.so once and declare its signatures.  Raises if it is missing."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not LIB_PATH.is_file():
+            raise ImportError(f"{LIB_PATH} not found: build it with `python -m emugen_b200.build`")
+        L = ctypes.CDLL(str(LIB_PATH))
+        vp, i32, i64 = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64
+        L.emu_abi_version.restype = i32
+        L.emu_abi_version.argtypes = []
+        L.emu_last_error.restype = ctypes.c_char_p
+        L.emu_last_error.argtypes = []
+        L.emu_status_string.restype = ctypes.c_char_p
+        L.emu_status_string.argtypes = [i32]
+        L.emu_gemm.restype = i32
+        L.emu_gemm.argtypes = [vp, vp, vp, vp, i64, i64, i64, i64, i64, i64, i64, vp,
+                               ctypes.POINTER(EmuGemmParams), vp, vp]
+        L.emu_nvfp4_global_scales.restype = i32
+        L.emu_nvfp4_global_scales.argtypes = [vp, i64, vp, i64, i32, vp, vp, vp, vp]
+        L.emu_quant_nvfp4.restype = i32
+        L.emu_quant_nvfp4.argtypes = [vp, i32, i64, i64, vp, vp, vp, vp]
+        L.emu_quant_mxfp4.restype = i32
+        L.emu_quant_mxfp4.argtypes = [vp, i32, i64, i64, vp, vp, vp]
+        v = L.emu_abi_version()
+        if v != ABI_VERSION:
+            raise ImportError(f"libemugen ABI version {v}, expected {ABI_VERSION}: rebuild it")
+        _lib = L
+    return _lib
+
+
+def _check(status: int) -> None:
+    if status != EMU_OK:
+        L = load()
+        raise EmuError(status, L.emu_last_error().decode() or L.emu_status_string(status).decode())
+
+
+def _device_for(*tensors: torch.Tensor) -> torch.device:
+    for t in tensors:
+        if t.is_cuda:
+            return t.device
+    if not torch.cuda.is_available():
+        raise RuntimeError("emugen_b200 needs a CUDA device (sm_100a); no CPU fallback exists")
+    return torch.device("cuda", torch.cuda.current_device())
+
+
+def _stream(dev: torch.device) -> int:
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+def _bytes2d(t: torch.Tensor, dev: torch.device, name: str) -> torch.Tensor:
+    if t.dim() != 2:
+        raise RuntimeError(f"{name} must be 2D")
+    if t.element_size() != 1:
+        raise RuntimeError(f"{name} must be a 1-byte dtype (uint8 / float8), got {t.dtype}")
+    return t.to(dev).contiguous().view(torch.uint8)
+
+
+def gemm(a_fp4: torch.Tensor, b_fp4: torch.Tensor, scale_a: torch.Tensor, scale_b: torch.Tensor, *,
+         fmt: int, group_size: int, w_reduce: int, stage3_rounding: int, stage4_rounding: int,
+         alpha: torch.Tensor | None, out_mode: int) -> torch.Tensor:
+    """Emulated scaled FP4 GEMM through ``emu_gemm``.  Returns [M, N] fp16 / bf16 / f32 on the
+    inputs' CUDA device (or on CPU if every input was on CPU)."""
+    L = load()
+    on_cpu = not any(t.is_cuda for t in (a_fp4, b_fp4, scale_a, scale_b))
+    dev = _device_for(a_fp4, b_fp4, scale_a, scale_b)
+    if a_fp4.dim() != 2 or b_fp4.dim() != 2:
+        raise RuntimeError("a_fp4, b_fp4 must be 2D")
+    M, N, K = a_fp4.shape[0], b_fp4.shape[0], a_fp4.shape[1] * 2
+    if b_fp4.shape[1] * 2 != K:
+        raise RuntimeError("K mismatch between a and b")
+    a = _bytes2d(a_fp4, dev, "a_fp4")
+    b = _bytes2d(b_fp4, dev, "b_fp4")
+    if scale_a.dim() != 2 or scale_b.dim() != 2:
+        raise RuntimeError("scale tensor must be 2D")
+    sa = _bytes2d(scale_a, dev, "scale_a")
+    sb = _bytes2d(scale_b, dev, "scale_b")
+    al = None
+    if alpha is not None:
+        if alpha.numel() != 1:
+            raise RuntimeError(f"a Tensor with {alpha.numel()} elements cannot be converted to Scalar")
+        al = alpha.detach().reshape(1).to(device=dev, dtype=torch.float32).contiguous()
+    odt = {EMU_OUT_F16: torch.float16, EMU_OUT_BF16_VIA_F16: torch.bfloat16, EMU_OUT_F32: torch.float32}[out_mode]
+    out = torch.empty((M, N), dtype=odt, device=dev)
+    params = EmuGemmParams(fmt, group_size, w_reduce, stage3_rounding, stage4_rounding, out_mode)
+    with torch.cuda.device(dev):
+        st = L.emu_gemm(a.data_ptr(), b.data_ptr(), sa.data_ptr(), sb.data_ptr(), M, N, K,
+                        sa.shape[0], sa.shape[1], sb.shape[0], sb.shape[1],
+                        None if al is None else al.data_ptr(), ctypes.byref(params), out.data_ptr(),
+                        _stream(dev))
+    _check(st)
+    return out.cpu() if on_cpu else out
+
+
+def _dtype_code(x: torch.Tensor) -> int:
+    if x.dtype == torch.float16:
+        return EMU_DTYPE_F16
+    if x.dtype == torch.bfloat16:
+        return EMU_DTYPE_BF16
+    raise RuntimeError(f"quantiser input must be float16 or bfloat16, got {x.dtype}")
+
+
+def nvfp4_global_scales(a: torch.Tensor, b: torch.Tensor):
+    """(gs_a, gs_b, alpha) as device float32[1] tensors, computed on the device."""
+    L = load()
+    dev = _device_for(a, b)
+    if a.dtype != b.dtype:
+        raise RuntimeError("a and b must have the same dtype")
+    a_ = a.to(dev).contiguous()
+    b_ = b.to(dev).contiguous()
+    gsa = torch.empty(1, dtype=torch.float32, device=dev)
+    gsb = torch.empty(1, dtype=torch.float32, device=dev)
+    al = torch.empty(1, dtype=torch.float32, device=dev)
+    with torch.cuda.device(dev):
+        st = L.emu_nvfp4_global_scales(a_.data_ptr(), a_.numel(), b_.data_ptr(), b_.numel(), _dtype_code(a_),
+                                       gsa.data_ptr(), gsb.data_ptr(), al.data_ptr(), _stream(dev))
+    _check(st)
+    return gsa, gsb, al
+
+
+def _quant(x: torch.Tensor, sf_vec: int, gs: torch.Tensor | None):
+    L = load()
+    dev = _device_for(x)
+    if x.dim() != 2:
+        x = x.reshape(-1, x.shape[-1])
+    x_ = x.to(dev).contiguous()
+    M, K = x_.shape
+    if K % sf_vec != 0:
+        raise RuntimeError(f"K must be a multiple of {sf_vec}")
+    q = torch.empty((M, K // 2), dtype=torch.uint8, device=dev)
+    rows = (M + 127) // 128 * 128
+    cols = (K // sf_vec + 3) // 4 * 4
+    sf = torch.empty((rows, cols), dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        if sf_vec == 16:
+            g = gs.reshape(1).to(device=dev, dtype=torch.float32).contiguous()
+            st = L.emu_quant_nvfp4(x_.data_ptr(), _dtype_code(x_), M, K, g.data_ptr(), q.data_ptr(), sf.data_ptr(),
+                                   _stream(dev))
+        else:
+            st = L.emu_quant_mxfp4(x_.data_ptr(), _dtype_code(x_), M, K, q.data_ptr(), sf.data_ptr(), _stream(dev))
+    _check(st)
+    return q, sf
+
+
+def quant_nvfp4(x: torch.Tensor, global_scale: torch.Tensor):
+    """x [M, K] fp16/bf16 -> (q uint8 [M, K/2], sf uint8 [pad128(M), pad4(K/16)] swizzled E4M3)."""
+    return _quant(x, 16, global_scale)
+
+
+def quant_mxfp4(x: torch.Tensor):
+    """x [M, K] fp16/bf16 -> (q uint8 [M, K/2], sf uint8 [pad128(M), pad4(K/32)] swizzled UE8M0)."""
+    return _quant(x, 32, None)

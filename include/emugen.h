@@ -1,0 +1,138 @@
+/*
+ * emugen.h — C ABI of libemugen.so, the B200 (sm_100a) implementation of EmuGen's emulated
+ * NVFP4 / MXFP4 scaled GEMM and of the FP4 quantisation that feeds it.
+ *
+ * Conventions (every entry point):
+ *   - All tensor arguments are DEVICE pointers owned by the caller; nothing is allocated or freed
+ *     on the caller's behalf.  Row-major, contiguous.
+ *   - Work is enqueued on `stream` (a cudaStream_t passed as void*; NULL = legacy default stream)
+ *     and returns without synchronising.  Device-resident scalars (alpha, global scales) are read
+ *     on the device, so no host round trip happens (the reference reads alpha with `.item()`).
+ *   - The return value is an emu_status; on failure emu_last_error() gives a message (thread-local)
+ *     whose text matches the reference's TORCH_CHECK message where the reference has one.
+ *   - Calls are reentrant; calls on different streams may overlap.
+ *
+ * Packed FP4 operands: [rows][K/2] bytes, element 2j in the low nibble of byte j, element 2j+1 in
+ * the high nibble; e2m1 codes, bit 3 = sign (reference nvfp_emulation.cpp:7-13, 29-39).
+ * Block scales: the 128x4 swizzled layout, a [rows_pad][cols_pad] byte buffer with rows_pad a
+ * multiple of 128 and cols_pad a multiple of 4; byte (r, c) sits at
+ *   (r/128)*(cols_pad/4)*512 + (c/4)*512 + (r%32)*16 + ((r%128)/32)*4 + c%4
+ * (reference nvfp_emulation.cpp:15-27; writer flashinfer quantization_utils.cuh:626-666).
+ */
+#ifndef EMUGEN_H_
+#define EMUGEN_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define EMU_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define EMU_API __attribute__((visibility("default")))
+#else
+#define EMU_API
+#endif
+
+typedef int32_t emu_status;
+enum {
+  EMU_OK = 0,
+  EMU_ERR_INVALID_ARGUMENT = 1,   /* null pointer, negative size, unknown enum value            */
+  EMU_ERR_K_MISMATCH = 2,         /* "K mismatch between a and b"                               */
+  EMU_ERR_K_GROUP = 3,            /* "K must be multiple of 16" / "K must be divisible by group_size" */
+  EMU_ERR_W_REDUCE = 4,           /* "G = K/16 must be multiple of 4" (generic: of w_reduce)     */
+  EMU_ERR_GROUP_SIZE = 5,         /* "only MXFP4 group_size=32 is supported" (and NVFP4: 16)     */
+  EMU_ERR_SCALE_SHAPE = 6,        /* "swizzled scale shape must be divisible by 128 and 4"        */
+  EMU_ERR_SCALE_TOO_SMALL = 7,    /* scale buffer has fewer rows / columns than M,N / K/group     */
+  EMU_ERR_UNSUPPORTED = 8,        /* a size beyond what this build supports (message says which)  */
+  EMU_ERR_CUDA = 9                /* a CUDA runtime error (message carries cudaGetErrorString)    */
+};
+
+/* Element formats. */
+enum { EMU_FMT_NVFP4 = 0, /* E4M3 block scales, group 16, stage-2 product in f32 */
+       EMU_FMT_MXFP4 = 1  /* UE8M0 block scales, group 32, stage-2 product in f64 */ };
+enum { EMU_RZ = 0, EMU_RNE = 1 };   /* same codes as nvfp_cpp_emul.RZ / RNE */
+enum { EMU_OUT_F16 = 0,             /* fp16, the C++ emulators' output */
+       EMU_OUT_BF16_VIA_F16 = 1,    /* bf16(fp16(x)): reference `.to(out_dtype)` after fp16, gemm.py:69 */
+       EMU_OUT_F32 = 2 };           /* the f32 accumulator times alpha, before the fp16 rounding */
+enum { EMU_DTYPE_F16 = 0, EMU_DTYPE_BF16 = 1 };  /* quantiser input dtypes */
+
+/* Accumulator model of one emulated GEMM (search/emulation/config.py:10-81 and the state fields
+ * of gemm_compare/backends/nvfp.py:30-44, mxfp.py:27-42).  w_stage3 / w_stage4 / m_chunk_size are
+ * absent on purpose: the reference keeps them for API compatibility and they change no result
+ * (search/emulation/core.py:31-38). */
+typedef struct emu_gemm_params {
+  int32_t format;           /* EMU_FMT_NVFP4 or EMU_FMT_MXFP4                                 */
+  int32_t group_size;       /* elements per block scale: 16 (NVFP4) or 32 (MXFP4)             */
+  int32_t w_reduce;         /* groups summed exactly in stage 3 (reference: 4 NVFP, 2 MXFP), 1..64 */
+  int32_t stage3_rounding;  /* EMU_RZ / EMU_RNE, used when K/group == w_reduce (one block)    */
+  int32_t stage4_rounding;  /* EMU_RZ / EMU_RNE, the running f32 accumulator                  */
+  int32_t out_mode;         /* EMU_OUT_*                                                      */
+} emu_gemm_params;
+
+/* ABI version of the loaded library (EMU_ABI_VERSION it was built with). */
+EMU_API int32_t emu_abi_version(void);
+
+/* Message of the last failing call on this thread ("" if none). */
+EMU_API const char* emu_last_error(void);
+
+/* Name of a status code. */
+EMU_API const char* emu_status_string(emu_status s);
+
+/*
+ * Emulated scaled FP4 GEMM:  out[M][N] = emul(A[M][K] x B[N][K]^T).
+ * Replaces:
+ *   nvfp_cpp_emul/nvfp_cpp_emul/csrc/nvfp_emulation.cpp:90-156  emulated_scaled_fp4_mm
+ *       (params {NVFP4, 16, 4, r3, r4, EMU_OUT_F16}, alpha = state.alpha)
+ *   mxfp_cpp_emul/mxfp_cpp_emul/csrc/mxfp_emulation.cpp:98-166  emulated_mxfp4_mm
+ *       (params {MXFP4, 32, 2, r3, r4, EMU_OUT_F16}, alpha = NULL)
+ *   search/emulation/core.py:69-148 MMAEngine.emulation_scaled_fp4_mm + gemm.py:35-69
+ *       emulate_nvfp_scaled_fp4_mm (generic w_reduce; EMU_OUT_BF16_VIA_F16 for bf16 out_dtype)
+ * a_fp4 [M][K/2], b_fp4 [N][K/2]; scale_a [scale_a_rows][scale_a_cols], scale_b likewise (swizzled);
+ * alpha: device float[1] multiplied into the f32 result (NULL = no multiply);
+ * out: [M][N] uint16 bits (fp16 / bf16) or float (EMU_OUT_F32).
+ * M, N >= 1; K >= 1 a multiple of group_size; (K/group_size) a multiple of w_reduce.
+ */
+EMU_API emu_status emu_gemm(const uint8_t* a_fp4, const uint8_t* b_fp4, const uint8_t* scale_a,
+                    const uint8_t* scale_b, int64_t M, int64_t N, int64_t K, int64_t scale_a_rows,
+                    int64_t scale_a_cols, int64_t scale_b_rows, int64_t scale_b_cols,
+                    const float* alpha, const emu_gemm_params* params, void* out, void* stream);
+
+/*
+ * NVFP4 global scale and GEMM alpha, on the device, without host synchronisation.
+ * Replaces gemm_compare/backends/nvfp.py:24-27 global_scale_nvfp and nvfp.py:174-177:
+ *   gs = f32(2688.0 / amax) in double, amax = max|x| (1.0 when amax is 0 or NaN),
+ *   alpha = f32(1.0 / max(gs_a * gs_b, 1e-8)) in double.
+ * a: [a_numel] fp16/bf16, b: [b_numel]; gs_a, gs_b, alpha: device float[1] outputs.
+ */
+EMU_API emu_status emu_nvfp4_global_scales(const void* a, int64_t a_numel, const void* b, int64_t b_numel,
+                                   int32_t dtype, float* gs_a, float* gs_b, float* alpha,
+                                   void* stream);
+
+/*
+ * NVFP4 quantisation: x [M][K] fp16/bf16 -> q [M][K/2] packed e2m1, sf [pad128(M)][pad4(K/16)]
+ * swizzled E4M3 block scales (padding written as 0).  global_scale: device float[1].
+ * Replaces nvfp.ops.scaled_fp4_quant at gemm_compare/backends/nvfp.py:178-179 (third-party,
+ * absent); the recipe is flashinfer fp4_quantize(x, gs, 16, sf_use_ue8m0=False, swizzled=True),
+ * flashinfer/data/csrc/nv_internal/tensorrt_llm/kernels/quantization_utils.cuh:352-366.
+ * K must be a multiple of 16.
+ */
+EMU_API emu_status emu_quant_nvfp4(const void* x, int32_t dtype, int64_t M, int64_t K,
+                           const float* global_scale, uint8_t* q, uint8_t* sf, void* stream);
+
+/*
+ * MXFP4 quantisation: x [M][K] fp16/bf16 -> q [M][K/2], sf [pad128(M)][pad4(K/32)] swizzled UE8M0.
+ * Replaces flashinfer.mxfp4_quantize at gemm_compare/backends/mxfp.py:199-200
+ * (flashinfer/quantization/fp4_quantization.py:1237-1282 -> quantization_utils.cuh:326-333).
+ * K must be a multiple of 32.
+ */
+EMU_API emu_status emu_quant_mxfp4(const void* x, int32_t dtype, int64_t M, int64_t K, uint8_t* q,
+                           uint8_t* sf, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* EMUGEN_H_ */

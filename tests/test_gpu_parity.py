@@ -1,0 +1,160 @@
+"""GPU parity: libemugen's emulated GEMM (through the C ABI, via the drop-in modules) against the
+reference's golden vectors and against the C oracle, bit for bit (NaN payloads excepted)."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle
+from tests.golden.make_golden import pad, quant_mxfp4_np, quant_nvfp4_np, swizzle
+from tests.golden_cases import load_cases, nan_equal_mismatches
+
+pytestmark = pytest.mark.gpu
+
+CASES = load_cases()
+
+
+def _bits(t: torch.Tensor) -> np.ndarray:
+    return t.detach().cpu().contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+@pytest.mark.parametrize("case", CASES, ids=[f"{c['id']}-{c['kind']}-{c['path']}-{c['data']}" for c in CASES])
+def test_golden_through_dropin(case):
+    from emugen_b200 import emulation, mxfp_cpp_emul, nvfp_cpp_emul
+
+    dev = "cuda"
+    a = torch.from_numpy(case["a"]).to(dev)
+    b = torch.from_numpy(case["b"]).to(dev)
+    sfa = torch.from_numpy(case["sfa"]).to(dev)
+    sfb = torch.from_numpy(case["sfb"]).to(dev)
+    alpha = torch.tensor([case["alpha"]], dtype=torch.float32, device=dev)
+    if case["kind"] == "nvfp":
+        sfa, sfb = sfa.view(torch.float8_e4m3fn), sfb.view(torch.float8_e4m3fn)
+    if case["path"] == "cpp":
+        if case["kind"] == "nvfp":
+            out = nvfp_cpp_emul.emulated_scaled_fp4_mm(a, b, sfa, sfb, alpha, 128, case["r3"], case["r4"])
+        else:
+            out = mxfp_cpp_emul.emulated_mxfp4_mm(a, b, sfa, sfb, 32, 128, case["r3"], case["r4"])
+    else:
+        st = emulation.SearchNVFPEmulationState(
+            a_fp4=a, b_fp4=b, scale_a=sfa, scale_b=sfb, alpha=alpha, out_dtype=getattr(torch, case["out_dtype"]),
+            w_stage3=25, w_stage4=25, w_reduce=case["w_reduce"], group_size=16 if case["kind"] == "nvfp" else 32,
+            m_chunk_size=128, stage3_rounding=case["r3"], stage4_rounding=case["r4"])
+        out = emulation.emulate_nvfp_scaled_fp4_mm(st)
+    assert out.dtype == getattr(torch, case["out_dtype"])
+    assert out.is_cuda and out.shape == (case["M"], case["N"])
+    assert nan_equal_mismatches(_bits(out), case["out"], case["out_dtype"]) == 0
+
+
+def _random_case(rng, fmt, M, N, K, data="quant"):
+    gs = 16 if fmt == "nvfp" else 32
+    G = K // gs
+    if data == "quant":
+        xa = rng.standard_normal((M, K)) * np.exp(rng.standard_normal((M, 1)))
+        xb = rng.standard_normal((N, K))
+        if fmt == "nvfp":
+            ga = np.float32(2688.0 / np.abs(xa).max())
+            gb = np.float32(2688.0 / np.abs(xb).max())
+            a, sa = quant_nvfp4_np(xa, ga)
+            b, sb = quant_nvfp4_np(xb, gb)
+        else:
+            a, sa = quant_mxfp4_np(xa)
+            b, sb = quant_mxfp4_np(xb)
+    else:
+        a = rng.integers(0, 256, (M, K // 2), dtype=np.uint8)
+        b = rng.integers(0, 256, (N, K // 2), dtype=np.uint8)
+        lo, hi = (0x20, 0x58) if fmt == "nvfp" else (110, 140)
+        sa = rng.integers(lo, hi, (M, G), dtype=np.uint8)
+        sb = rng.integers(lo, hi, (N, G), dtype=np.uint8)
+    return a, b, swizzle(sa, pad(M, 128), pad(G, 4)), swizzle(sb, pad(N, 128), pad(G, 4))
+
+
+def _run_lib(a, b, sfa, sfb, fmt, wr, r3, r4, alpha, out_mode):
+    from emugen_b200 import _lib
+
+    dev = "cuda"
+    al = None if alpha is None else torch.tensor([alpha], dtype=torch.float32, device=dev)
+    return _lib.gemm(torch.from_numpy(a).to(dev), torch.from_numpy(b).to(dev), torch.from_numpy(sfa).to(dev),
+                     torch.from_numpy(sfb).to(dev), fmt=0 if fmt == "nvfp" else 1, group_size=16 if fmt == "nvfp" else 32,
+                     w_reduce=wr, stage3_rounding=r3, stage4_rounding=r4, alpha=al, out_mode=out_mode)
+
+
+GRID = [
+    # fmt, M, N, K, w_reduce, r3, r4, out_mode, data
+    ("nvfp", 256, 192, 1024, 4, 0, 0, 0, "quant"),
+    ("nvfp", 129, 65, 512, 4, 1, 1, 1, "quant"),
+    ("nvfp", 7, 300, 2048, 4, 0, 1, 2, "quant"),
+    ("nvfp", 64, 64, 256, 1, 0, 0, 0, "raw"),
+    ("nvfp", 64, 64, 768, 3, 1, 0, 2, "raw"),
+    ("nvfp", 33, 31, 4096, 16, 0, 0, 0, "quant"),
+    ("nvfp", 200, 100, 64, 4, 1, 1, 0, "raw"),
+    ("mxfp", 256, 192, 1024, 2, 0, 0, 0, "quant"),
+    ("mxfp", 129, 65, 512, 2, 1, 1, 1, "quant"),
+    ("mxfp", 7, 300, 2048, 2, 0, 1, 2, "quant"),
+    ("mxfp", 64, 64, 256, 1, 0, 0, 0, "raw"),
+    ("mxfp", 64, 64, 768, 3, 1, 0, 2, "raw"),
+    ("mxfp", 200, 100, 64, 2, 1, 1, 0, "raw"),
+]
+
+
+@pytest.mark.parametrize("fmt,M,N,K,wr,r3,r4,out_mode,data", GRID)
+def test_random_vs_oracle(fmt, M, N, K, wr, r3, r4, out_mode, data):
+    rng = np.random.default_rng(hash((fmt, M, N, K, wr, r3, r4, out_mode)) & 0xFFFFFFFF)
+    a, b, sfa, sfb = _random_case(rng, fmt, M, N, K, data)
+    alpha = float(np.float32(rng.uniform(1e-5, 1e-2))) if fmt == "nvfp" else None
+    got = _run_lib(a, b, sfa, sfb, fmt, wr, r3, r4, alpha, out_mode)
+    ref = oracle.emul_gemm(a, b, sfa, sfb, scale_fmt=0 if fmt == "nvfp" else 1, group_size=16 if fmt == "nvfp" else 32,
+                           w_reduce=wr, r3=r3, r4=r4, alpha=alpha, out_mode=out_mode)
+    if out_mode == 2:
+        g = got.cpu().numpy()
+        assert np.array_equal(g.view(np.uint32), ref.view(np.uint32)) or \
+            np.array_equal(np.isnan(g), np.isnan(ref)) and np.array_equal(g[~np.isnan(g)].view(np.uint32),
+                                                                          ref[~np.isnan(ref)].view(np.uint32))
+    else:
+        assert nan_equal_mismatches(_bits(got), ref, "bfloat16" if out_mode == 1 else "float16") == 0
+
+
+@pytest.mark.parametrize("fmt", ["nvfp", "mxfp"])
+def test_sampled_elements_at_4096(fmt):
+    """Full-size kernel launch (4096^3); 96 sampled outputs re-derived by the oracle on the
+    corresponding row / column slices (the oracle is too slow for the whole product)."""
+    rng = np.random.default_rng(7 if fmt == "nvfp" else 8)
+    M = N = K = 4096
+    a, b, sfa, sfb = _random_case(rng, fmt, M, N, K, "quant")
+    alpha = 1e-3 if fmt == "nvfp" else None
+    got = _bits(_run_lib(a, b, sfa, sfb, fmt, 4 if fmt == "nvfp" else 2, 0, 0, alpha, 0))
+    rows = rng.choice(M, 12, replace=False)
+    cols = rng.choice(N, 8, replace=False)
+    gsz = 16 if fmt == "nvfp" else 32
+    G = K // gsz
+
+    def unswz(buf, idx):
+        from tests.golden.make_golden import swizzle as _s  # noqa: F401
+
+        lin = np.empty((len(idx), G), dtype=np.uint8)
+        for i, r in enumerate(idx):
+            for g in range(G):
+                lin[i, g] = buf.reshape(-1)[oracle.swizzle_offset(int(r), g, buf.shape[1])]
+        return swizzle(lin, 128, pad(G, 4))
+
+    ref = oracle.emul_gemm(a[rows], b[cols], unswz(sfa, rows), unswz(sfb, cols), scale_fmt=0 if fmt == "nvfp" else 1,
+                           group_size=gsz, w_reduce=4 if fmt == "nvfp" else 2, alpha=alpha, out_mode=0)
+    assert nan_equal_mismatches(got[np.ix_(rows, cols)], ref, "float16") == 0
+
+
+def test_cpu_inputs_computed_on_gpu():
+    from emugen_b200 import nvfp_cpp_emul
+
+    c = CASES[0]
+    out = nvfp_cpp_emul.emulated_scaled_fp4_mm(torch.from_numpy(c["a"]), torch.from_numpy(c["b"]),
+                                               torch.from_numpy(c["sfa"]).view(torch.float8_e4m3fn),
+                                               torch.from_numpy(c["sfb"]).view(torch.float8_e4m3fn),
+                                               torch.tensor([c["alpha"]]), 128, c["r3"], c["r4"])
+    assert out.device.type == "cpu"
+    assert nan_equal_mismatches(_bits(out), c["out"], "float16") == 0
+
+
+def test_repeated_calls_are_deterministic():
+    c = CASES[1]
+    outs = [_bits(_run_lib(c["a"], c["b"], c["sfa"], c["sfb"], "nvfp", 4, c["r3"], c["r4"], c["alpha"], 0))
+            for _ in range(3)]
+    assert all((o == outs[0]).all() for o in outs)

@@ -1,0 +1,112 @@
+"""GPU tests of the FP4 quantisers: structure (layout, padding, nibble order) against exactly
+representable inputs, and bit parity with flashinfer's quantiser (the reference quant_fn's
+third-party implementation) when flashinfer can build its kernels on this machine."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle
+
+pytestmark = pytest.mark.gpu
+
+E2M1 = [0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0]
+
+
+def _exact_input(rng, M, K, gs, dtype):
+    """Values whose quantisation is exact: each block holds e2m1 values times 2^e with the max 6."""
+    codes = rng.integers(0, 16, (M, K)).astype(np.uint8)
+    codes[:, ::gs] = 7  # block max = 6 * 2^e
+    vals = np.array(E2M1)[codes & 7] * np.where(codes & 8, -1.0, 1.0)
+    e = rng.integers(-3, 4, (M, K // gs)).repeat(gs, axis=1)
+    x = vals * np.exp2(e)
+    return torch.from_numpy(x).to(dtype), codes, e[:, ::gs]
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("M,K", [(1, 64), (130, 256), (256, 4096)])
+def test_mxfp4_quant_exact_values(dtype, M, K):
+    from emugen_b200 import quant_mxfp4
+
+    rng = np.random.default_rng(M * K)
+    x, codes, e = _exact_input(rng, M, K, 32, dtype)
+    q, sf = quant_mxfp4(x.cuda())
+    q, sf = q.cpu().numpy(), sf.cpu().numpy()
+    exp_codes = codes.copy()
+    exp_codes[(codes & 7) == 0] = 0  # -0 quantises to +0 code? keep sign bit as produced below
+    lo, hi = q & 0xF, q >> 4
+    got = np.empty((M, K), dtype=np.uint8)
+    got[:, 0::2], got[:, 1::2] = lo, hi
+    nz = (codes & 7) != 0
+    assert np.array_equal(got[nz], codes[nz])
+    assert np.all((got[~nz] & 7) == 0)
+    G = K // 32
+    for r in range(0, M, max(1, M // 7)):
+        for g in range(G):
+            assert sf.reshape(-1)[oracle.swizzle_offset(r, g, sf.shape[1])] == 127 + e[r, g]
+    assert sf.shape == ((M + 127) // 128 * 128, (G + 3) // 4 * 4)
+
+
+def test_quant_padding_is_zero():
+    from emugen_b200 import quant_mxfp4, quant_nvfp4
+
+    x = torch.randn(130, 96, dtype=torch.float16, device="cuda")
+    _, sf = quant_mxfp4(x)  # 3 scale columns padded to 4, 130 rows padded to 256
+    s = sf.cpu().numpy().reshape(-1)
+    for r in range(256):
+        for c in range(4):
+            v = s[oracle.swizzle_offset(r, c, 4)]
+            if r >= 130 or c >= 3:
+                assert v == 0
+    gs = torch.tensor([1.0], device="cuda")
+    _, sf = quant_nvfp4(torch.randn(5, 80, dtype=torch.bfloat16, device="cuda"), gs)
+    s = sf.cpu().numpy().reshape(-1)
+    assert all(s[oracle.swizzle_offset(r, c, 8)] == 0 for r in range(128) for c in range(8) if r >= 5 or c >= 5)
+
+
+def _flashinfer_fp4_quantize():
+    try:
+        import flashinfer
+        from flashinfer import fp4_quantize
+        fp4_quantize(torch.randn(128, 64, dtype=torch.float16, device="cuda"), torch.tensor([1.0], device="cuda"),
+                     16, False, True)
+        return flashinfer
+    except Exception as e:  # flashinfer missing or its JIT build unavailable
+        pytest.skip(f"flashinfer fp4_quantize unavailable: {type(e).__name__}: {e}")
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("M,K", [(128, 256), (257, 1024), (1, 4096)])
+def test_quant_bit_parity_with_flashinfer(dtype, M, K):
+    fi = _flashinfer_fp4_quantize()
+    from emugen_b200 import nvfp4_global_scales, quant_mxfp4, quant_nvfp4
+
+    g = torch.Generator().manual_seed(M + K)
+    x = (torch.randn(M, K, generator=g) * torch.exp(torch.randn(M, 1, generator=g))).to(dtype).cuda()
+    x[0, :7] = 0
+    gs, _, _ = nvfp4_global_scales(x, x)
+    q_ref, sf_ref = fi.fp4_quantize(x, gs, 16, False, True)
+    q, sf = quant_nvfp4(x, gs)
+    assert torch.equal(q.cpu(), q_ref.view(torch.uint8).cpu())
+    assert torch.equal(sf.cpu().reshape(-1), sf_ref.view(torch.uint8).cpu().reshape(-1))
+    q_ref, sf_ref = fi.mxfp4_quantize(x)
+    q, sf = quant_mxfp4(x)
+    assert torch.equal(q.cpu(), q_ref.view(torch.uint8).cpu())
+    assert torch.equal(sf.cpu().reshape(-1), sf_ref.view(torch.uint8).cpu().reshape(-1))
+
+
+def test_global_scales_match_reference_recipe():
+    from emugen_b200 import nvfp4_global_scales
+
+    a = torch.randn(300, 500, dtype=torch.float16) * 3
+    b = torch.randn(200, 500, dtype=torch.float16)
+    gsa, gsb, alpha = nvfp4_global_scales(a.cuda(), b.cuda())
+    # reference gemm_compare/backends/nvfp.py:24-27, 176 in Python doubles
+    amax_a = torch.abs(a).max().to(torch.float32).item()
+    amax_b = torch.abs(b).max().to(torch.float32).item()
+    ga = np.float32(448.0 * 6.0 / (amax_a if amax_a > 0 else 1.0))
+    gb = np.float32(448.0 * 6.0 / (amax_b if amax_b > 0 else 1.0))
+    al = np.float32(1.0 / max(float(ga) * float(gb), 1e-8))
+    assert gsa.item() == float(ga) and gsb.item() == float(gb) and alpha.item() == float(al)
+    z = torch.zeros(4, 16, dtype=torch.bfloat16, device="cuda")
+    gz, _, _ = nvfp4_global_scales(z, z)
+    assert gz.item() == 2688.0
