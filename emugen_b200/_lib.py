@@ -24,8 +24,8 @@ EMU_OUT_F16, EMU_OUT_BF16_VIA_F16, EMU_OUT_F32 = 0, 1, 2
 EMU_DTYPE_F16, EMU_DTYPE_BF16 = 0, 1
 ABI_VERSION = 1
 
-SYMBOLS = ("emu_abi_version", "emu_last_error", "emu_status_string", "emu_gemm",
-           "emu_nvfp4_global_scales", "emu_quant_nvfp4", "emu_quant_mxfp4")
+SYMBOLS = ("emu_abi_version", "emu_last_error", "emu_status_string", "emu_gemm", "emu_gemm_workspace_size",
+           "emu_gemm_ws", "emu_nvfp4_global_scales", "emu_quant_nvfp4", "emu_quant_mxfp4")
 
 
 class EmuGemmParams(ctypes.Structure):
@@ -67,6 +67,11 @@ def load() -> ctypes.CDLL:
         L.emu_gemm.restype = i32
         L.emu_gemm.argtypes = [vp, vp, vp, vp, i64, i64, i64, i64, i64, i64, i64, vp,
                                ctypes.POINTER(EmuGemmParams), vp, vp]
+        L.emu_gemm_workspace_size.restype = ctypes.c_size_t
+        L.emu_gemm_workspace_size.argtypes = [i64, i64, i64, ctypes.POINTER(EmuGemmParams)]
+        L.emu_gemm_ws.restype = i32
+        L.emu_gemm_ws.argtypes = [vp, vp, vp, vp, i64, i64, i64, i64, i64, i64, i64, vp,
+                                  ctypes.POINTER(EmuGemmParams), vp, vp, ctypes.c_size_t, vp]
         L.emu_nvfp4_global_scales.restype = i32
         L.emu_nvfp4_global_scales.argtypes = [vp, i64, vp, i64, i32, vp, vp, vp, vp]
         L.emu_quant_nvfp4.restype = i32
@@ -109,9 +114,12 @@ def _bytes2d(t: torch.Tensor, dev: torch.device, name: str) -> torch.Tensor:
 
 def gemm(a_fp4: torch.Tensor, b_fp4: torch.Tensor, scale_a: torch.Tensor, scale_b: torch.Tensor, *,
          fmt: int, group_size: int, w_reduce: int, stage3_rounding: int, stage4_rounding: int,
-         alpha: torch.Tensor | None, out_mode: int) -> torch.Tensor:
-    """Emulated scaled FP4 GEMM through ``emu_gemm``.  Returns [M, N] fp16 / bf16 / f32 on the
-    inputs' CUDA device (or on CPU if every input was on CPU)."""
+         alpha: torch.Tensor | None, out_mode: int, path: str = "auto") -> torch.Tensor:
+    """Emulated scaled FP4 GEMM through ``emu_gemm_ws``.  Returns [M, N] fp16 / bf16 / f32 on the
+    inputs' CUDA device (or on CPU if every input was on CPU).
+
+    path: "auto" gives the library a workspace (tensor-core kernel where it applies); "simt" passes
+    none, which selects the CUDA-core kernel.  Both are bit-identical; "simt" exists for tests."""
     L = load()
     on_cpu = not any(t.is_cuda for t in (a_fp4, b_fp4, scale_a, scale_b))
     dev = _device_for(a_fp4, b_fp4, scale_a, scale_b)
@@ -134,11 +142,20 @@ def gemm(a_fp4: torch.Tensor, b_fp4: torch.Tensor, scale_a: torch.Tensor, scale_
     odt = {EMU_OUT_F16: torch.float16, EMU_OUT_BF16_VIA_F16: torch.bfloat16, EMU_OUT_F32: torch.float32}[out_mode]
     out = torch.empty((M, N), dtype=odt, device=dev)
     params = EmuGemmParams(fmt, group_size, w_reduce, stage3_rounding, stage4_rounding, out_mode)
+    ws_ptr, ws_bytes, ws = None, 0, None
+    if path == "auto" and M > 0 and N > 0 and K > 0:
+        need = L.emu_gemm_workspace_size(M, N, K, ctypes.byref(params))
+        if need:
+            ws = torch.empty(need + 1024, dtype=torch.uint8, device=dev)
+            ws_ptr = (ws.data_ptr() + 1023) // 1024 * 1024
+            ws_bytes = need
+    elif path not in ("auto", "simt"):
+        raise ValueError(f"unknown path {path!r}")
     with torch.cuda.device(dev):
-        st = L.emu_gemm(a.data_ptr(), b.data_ptr(), sa.data_ptr(), sb.data_ptr(), M, N, K,
-                        sa.shape[0], sa.shape[1], sb.shape[0], sb.shape[1],
-                        None if al is None else al.data_ptr(), ctypes.byref(params), out.data_ptr(),
-                        _stream(dev))
+        st = L.emu_gemm_ws(a.data_ptr(), b.data_ptr(), sa.data_ptr(), sb.data_ptr(), M, N, K,
+                           sa.shape[0], sa.shape[1], sb.shape[0], sb.shape[1],
+                           None if al is None else al.data_ptr(), ctypes.byref(params), out.data_ptr(),
+                           ws_ptr, ws_bytes, _stream(dev))
     _check(st)
     return out.cpu() if on_cpu else out
 

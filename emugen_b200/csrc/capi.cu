@@ -60,10 +60,8 @@ const char* emu_status_string(emu_status s) {
   }
 }
 
-emu_status emu_gemm(const uint8_t* a_fp4, const uint8_t* b_fp4, const uint8_t* scale_a,
-                    const uint8_t* scale_b, int64_t M, int64_t N, int64_t K, int64_t scale_a_rows,
-                    int64_t scale_a_cols, int64_t scale_b_rows, int64_t scale_b_cols,
-                    const float* alpha, const emu_gemm_params* params, void* out, void* stream) {
+static emu_status validate_gemm(int64_t M, int64_t N, int64_t K, int64_t scale_a_rows, int64_t scale_a_cols,
+                                int64_t scale_b_rows, int64_t scale_b_cols, const emu_gemm_params* params) {
   if (!params) return fail(EMU_ERR_INVALID_ARGUMENT, "params must not be NULL");
   const emu_gemm_params p = *params;
   if (M < 0 || N < 0 || K < 0) return fail(EMU_ERR_INVALID_ARGUMENT, "negative size");
@@ -103,18 +101,56 @@ emu_status emu_gemm(const uint8_t* a_fp4, const uint8_t* b_fp4, const uint8_t* s
     return fail(EMU_ERR_INVALID_ARGUMENT, "rounding must be EMU_RZ (0) or EMU_RNE (1)");
   if (p.out_mode < EMU_OUT_F16 || p.out_mode > EMU_OUT_F32)
     return fail(EMU_ERR_INVALID_ARGUMENT, "unknown out_mode %d", p.out_mode);
+  if ((N + 63) / 64 > 65535) return fail(EMU_ERR_UNSUPPORTED, "N too large for this build (max 4194240)");
+  return EMU_OK;
+}
+
+static bool tc_path(const emu_gemm_params& p, int64_t M, int64_t N, int64_t K) {
+  return emu::gemm_tc_supported(p.format, p.w_reduce, M, N, K);
+}
+
+size_t emu_gemm_workspace_size(int64_t M, int64_t N, int64_t K, const emu_gemm_params* params) {
+  if (!params || M <= 0 || N <= 0 || K <= 0) return 0;
+  if (params->group_size <= 0 || K % params->group_size != 0) return 0;
+  if (!tc_path(*params, M, N, K)) return 0;
+  return emu::gemm_tc_workspace_size(params->format, M, N, K);
+}
+
+emu_status emu_gemm_ws(const uint8_t* a_fp4, const uint8_t* b_fp4, const uint8_t* scale_a, const uint8_t* scale_b,
+                       int64_t M, int64_t N, int64_t K, int64_t scale_a_rows, int64_t scale_a_cols,
+                       int64_t scale_b_rows, int64_t scale_b_cols, const float* alpha, const emu_gemm_params* params,
+                       void* out, void* workspace, size_t workspace_bytes, void* stream) {
+  emu_status st = validate_gemm(M, N, K, scale_a_rows, scale_a_cols, scale_b_rows, scale_b_cols, params);
+  if (st != EMU_OK) return st;
   if (M == 0 || N == 0) return ok();
   if (!a_fp4 || !b_fp4 || !scale_a || !scale_b || !out)
     return fail(EMU_ERR_INVALID_ARGUMENT, "tensor pointers must not be NULL");
   if (!aligned(a_fp4, 16) || !aligned(b_fp4, 16))
     return fail(EMU_ERR_INVALID_ARGUMENT, "a_fp4 / b_fp4 must be 16-byte aligned");
-  if ((M + 63) / 64 > 0x7FFFFFFFll || (N + 63) / 64 > 65535)
-    return fail(EMU_ERR_UNSUPPORTED, "N too large for this build (max 4194240)");
-
+  const emu_gemm_params p = *params;
   emu::GemmArgs args{p.format, p.w_reduce, p.stage3_rounding, p.stage4_rounding, p.out_mode};
-  cudaError_t e = emu::launch_gemm_simt(a_fp4, b_fp4, scale_a, scale_b, M, N, K, scale_a_cols, scale_b_cols,
-                                        alpha, args, out, static_cast<cudaStream_t>(stream));
-  return cuda_status(e, "emu_gemm launch");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (workspace && tc_path(p, M, N, K)) {
+    if (!aligned(workspace, 1024))
+      return fail(EMU_ERR_INVALID_ARGUMENT, "workspace must be 1024-byte aligned");
+    if (workspace_bytes < emu::gemm_tc_workspace_size(p.format, M, N, K))
+      return fail(EMU_ERR_INVALID_ARGUMENT, "workspace too small: %zu < %zu bytes", workspace_bytes,
+                  emu::gemm_tc_workspace_size(p.format, M, N, K));
+    return cuda_status(emu::launch_gemm_tc(a_fp4, b_fp4, scale_a, scale_b, M, N, K, scale_a_cols, scale_b_cols, alpha,
+                                           args, out, workspace, s),
+                       "emu_gemm tensor-core launch");
+  }
+  return cuda_status(emu::launch_gemm_simt(a_fp4, b_fp4, scale_a, scale_b, M, N, K, scale_a_cols, scale_b_cols, alpha,
+                                           args, out, s),
+                     "emu_gemm launch");
+}
+
+emu_status emu_gemm(const uint8_t* a_fp4, const uint8_t* b_fp4, const uint8_t* scale_a,
+                    const uint8_t* scale_b, int64_t M, int64_t N, int64_t K, int64_t scale_a_rows,
+                    int64_t scale_a_cols, int64_t scale_b_rows, int64_t scale_b_cols,
+                    const float* alpha, const emu_gemm_params* params, void* out, void* stream) {
+  return emu_gemm_ws(a_fp4, b_fp4, scale_a, scale_b, M, N, K, scale_a_rows, scale_a_cols, scale_b_rows, scale_b_cols,
+                     alpha, params, out, nullptr, 0, stream);
 }
 
 emu_status emu_nvfp4_global_scales(const void* a, int64_t a_numel, const void* b, int64_t b_numel,

@@ -19,6 +19,13 @@ cudaError_t launch_gemm_simt(const uint8_t* A, const uint8_t* B, const uint8_t* 
                              int64_t M, int64_t N, int64_t K, int64_t sa_cols, int64_t sb_cols,
                              const float* alpha, const GemmArgs& args, void* out, cudaStream_t stream);
 
+size_t gemm_tc_workspace_size(int fmt, int64_t M, int64_t N, int64_t K);
+bool gemm_tc_supported(int fmt, int w_reduce, int64_t M, int64_t N, int64_t K);
+cudaError_t launch_gemm_tc(const uint8_t* A, const uint8_t* B, const uint8_t* SA, const uint8_t* SB,
+                           int64_t M, int64_t N, int64_t K, int64_t sa_cols, int64_t sb_cols,
+                           const float* alpha, const GemmArgs& args, void* out, void* workspace,
+                           cudaStream_t stream);
+
 cudaError_t launch_quant(int sf_vec, const void* x, int dtype, int64_t M, int64_t K,
                          const float* global_scale, uint8_t* q, uint8_t* sf, cudaStream_t stream);
 

@@ -22,6 +22,7 @@
 #ifndef EMUGEN_H_
 #define EMUGEN_H_
 
+#include <stddef.h>
 #include <stdint.h>
 
 #ifdef __cplusplus
@@ -99,6 +100,26 @@ EMU_API emu_status emu_gemm(const uint8_t* a_fp4, const uint8_t* b_fp4, const ui
                     const uint8_t* scale_b, int64_t M, int64_t N, int64_t K, int64_t scale_a_rows,
                     int64_t scale_a_cols, int64_t scale_b_rows, int64_t scale_b_cols,
                     const float* alpha, const emu_gemm_params* params, void* out, void* stream);
+
+/*
+ * Bytes of device workspace emu_gemm_ws needs to take the tensor-core path for this problem
+ * (0 when the problem runs on the CUDA-core path, which needs none).  The tensor-core path covers
+ * the reference's accumulator shapes (NVFP4 w_reduce 4, MXFP4 w_reduce 2) with K a multiple of 64.
+ */
+EMU_API size_t emu_gemm_workspace_size(int64_t M, int64_t N, int64_t K, const emu_gemm_params* params);
+
+/*
+ * emu_gemm with caller-provided scratch: `workspace` (1024-byte aligned, at least
+ * emu_gemm_workspace_size bytes, contents need not be initialised) enables the tcgen05 path; with
+ * workspace == NULL the call is exactly emu_gemm.  Same results bit for bit either way.
+ * Replaces the same reference entry points as emu_gemm.  The workspace must not be used by
+ * another call until this one has completed on `stream`.
+ */
+EMU_API emu_status emu_gemm_ws(const uint8_t* a_fp4, const uint8_t* b_fp4, const uint8_t* scale_a,
+                       const uint8_t* scale_b, int64_t M, int64_t N, int64_t K, int64_t scale_a_rows,
+                       int64_t scale_a_cols, int64_t scale_b_rows, int64_t scale_b_cols,
+                       const float* alpha, const emu_gemm_params* params, void* out,
+                       void* workspace, size_t workspace_bytes, void* stream);
 
 /*
  * NVFP4 global scale and GEMM alpha, on the device, without host synchronisation.
