@@ -1,38 +1,47 @@
 // Emulated scaled FP4 GEMM on the 5th-generation tensor cores (tcgen05 + TMEM + TMA), sm_100a.
 //
-// Stage 1 (the exact group dot products) runs on the tensor core; stages 2-4 (scale, exact f64
-// group sums, RZ/RNE accumulation) run on CUDA cores reading TMEM.  Bit-exact to the reference
-// emulators (nvfp_emulation.cpp:90-156, mxfp_emulation.cpp:98-166) for the reference's accumulator
-// shapes: NVFP4 w_reduce 4 and MXFP4 w_reduce 2 (one 64-element K block per stage-3 sum).
+// Stage 1 (the exact group dot products) runs on the tensor core; stages 2-4 (scale, exact group sums,
+// RZ/RNE accumulation) run on CUDA cores reading TMEM.  Bit-exact to the reference emulators
+// (nvfp_emulation.cpp:90-156, mxfp_emulation.cpp:98-166) for the reference's accumulator shapes:
+// NVFP4 w_reduce 4 and MXFP4 w_reduce 2 (one 64-element K block per stage-3 sum).
 //
-// Pre-pass (one launch per operand):  packed e2m1 -> fp16 "2x" integers (0, +-1 .. +-12, exact),
-// and per-row / per-column scale tables in the form the epilogue consumes.
+// Pre-pass kernels (per call):
+//   unpack_stats    packed e2m1 -> fp16 "2x" integers (exact), plus per (row, group) the L1 and
+//                   max norms of the 2x values, which bound |p4| = |4 * group dot| from above.
+//   row / col       scale tables for both epilogue paths (below) and per-(row|col, block) exponent
+//                   bases; column tables are laid out per (block, 64-column tile) so one bulk copy
+//                   brings a block's column data into shared memory.
+//   tile stats      per (128-row | 64-column tile, group) maxima of the norms and multipliers.
+//   decide          per (row tile, column tile, block): integer path or f64 path (below).
 //
-// Main kernel: persistent, one CTA per SM, 10 warps:
-//   warp 0      TMA producer: A tile [128 x 64] and B tile [64 x 64] fp16 per K block into a
-//               6-stage shared-memory ring (128-byte swizzle), B-side scale table [groups x 64]
-//               f64 into a 4-stage ring.
-//   warp 1      TMEM owner + MMA issuer: per group one tcgen05.mma kind::f16 M128 N64 K16
-//               (NVFP4; MXFP4 groups take two, accumulated) into its own TMEM accumulator, so
-//               TMEM holds p4 = 4 * (exact group dot) for every (row, column, group) in f32.
-//   warps 2-9   epilogue: each thread owns one output row (its TMEM lane) and 32 columns.
-// TMEM: 512 columns = ring of accumulator sets, one set per K block (NVFP4: 4 groups x 64 columns,
-// two sets; MXFP4: 2 x 64, four sets), so the MMA of block b+1 overlaps the epilogue of block b.
+// Main kernel: persistent, one CTA per SM, 2 + EPI warps:
+//   warp 0      producer: TMA A [128 x 64] and B [64 x 64] fp16 tiles (128-byte swizzle) into a
+//               6-stage ring; one bulk copy of the block's column record into a 4-stage ring.
+//   warp 1      TMEM owner + MMA issuer: per group one tcgen05.mma kind::f16 M128 N64 K16 (NVFP4;
+//               MXFP4 groups take two, accumulated) into its own TMEM accumulator, so TMEM holds
+//               p4 for every (row, column, group) of the block.  512 columns = a ring of K-block
+//               sets (NVFP4: 2 sets of 4 x 64; MXFP4: 4 sets of 2 x 64).
+//   warps 2..   epilogue (EPI = 8 or 16 warps): a thread owns one output row (its TMEM lane) and
+//               64 / (EPI/4) columns.
 //
-// Epilogue arithmetic per group partial (exact; conversions into 64-bit types avoided because
-// they run at a quarter of the FP64 rate on B200):
-//   NVFP4: bits = FFMA(p4, ma, 1.5*2^23)            (integer p4*ma in the f32 mantissa, exact)
-//          d    = double{hi = 2^E exponent word of the row scale, lo = bits}
-//          diff = d - double{hi, 0x4B400000}        = p * sa exactly
-//          S    = FMA(diff, sb, S)                  (f64; the 4-group sum is exact)
-//   MXFP4: diff = double{2^52, FADD(p4, 1.5*2^23)} - (2^52 + 0x4B400000)  = p4 exactly
-//          S    = FMA(diff * (2^(ua-127)/4), 2^(ub-127), S)   (inf / NaN follow IEEE as in the reference)
-//   block: acc = R4(f64(acc) + S)  (first block: R4(S); single block: R3(S))
-// A stage-1 group sum of magnitude >= 512 is rounded to the fp16 grid first; a per-warp max test
-// sends those (rare) cases through the rounding routine.
+// Integer path (blocks whose tile bounds prove it exact):  per group partial
+//     bits = FFMA(p4, ma * 2^(ea_g - ea), 1.5*2^23)   integer t = p4 * ma * 2^.. in the f32 mantissa
+//     S32  = IMAD(bits, mb * 2^(eb_g - eb), S32)     int32, wraps; the 2^23 bias is removed per block
+//   per block:  T = S32 + K_col (exact integer), Tf = double{2^52, T} - (2^52 + 2^31),
+//     acc = R4(FMA(Tf, 2^ea_row * 2^eb_col, acc))   with the exponent bases of the row and column.
+//   Exactness needs no fp16 rounding (|p4| < 2048), |t| < 2^22 and |T| < 2^31; the decide kernel
+//   checks these with |p4| <= min(L1a*maxb, maxa*L1b) on tile maxima.
+// f64 path (any other block):  per group partial
+//     NVFP4: diff = double{2^E(sa), FFMA(p4, ma, 1.5*2^23)} - double{2^E(sa), 2^23 bias} = p*sa
+//            S = FMA(diff, sb, S)
+//     MXFP4: p4 exactly as f64 by the same construction; S = FMA(p4 * sa/4, sb, S)  (inf/NaN as IEEE)
+//   with stage-1 fp16 rounding applied when a warp sees |p4| >= 2048.
+// Conversions into 64-bit types are never used per partial: they run at a quarter of the FP64 rate.
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+
+#include <stdlib.h>
 
 #include <algorithm>
 
@@ -44,104 +53,286 @@ namespace emu {
 namespace tc {
 
 constexpr int BM = 128, BN = 64, BK = 64;
-constexpr int NSTAGE = 6, NSB = 4;
-constexpr int NUM_THREADS = 320;                  // 10 warps
+constexpr int NSTAGE = 6, NCR = 4;
 constexpr int A_BYTES = BM * BK * 2, B_BYTES = BN * BK * 2;
-constexpr int STAGE_BYTES = A_BYTES + B_BYTES;    // 24 KB
-constexpr int SB_BYTES = 4 * BN * 8;              // up to 4 groups x 64 columns x f64
-constexpr float MAGIC_F = 12582912.0f;            // 1.5 * 2^23
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;          // 24 KB
+constexpr float MAGIC_F = 12582912.0f;                  // 1.5 * 2^23
 constexpr uint32_t MAGIC_BITS = 0x4B400000u;
-constexpr int GROUP_M = 16;                       // tile raster: 16 M-tiles per band
-constexpr int SMEM_BYTES = 1024 /*align*/ + NSTAGE * STAGE_BYTES + NSB * SB_BYTES + 256;
+constexpr double TWO52 = 4503599627370496.0;
+constexpr int GROUP_M = 16;                             // tile raster: 16 M-tiles per band
 
-// NVFP4 row-scale record, one per (row, group).
+// Column record of one (K block, 64-column tile), GPB groups:
+//   int32  sbq[4][64]   mb * 2^(eb_g - eb)                       (integer path)
+//   uint32 kc[64]       2^31 - 2^23-bias * sum_g sbq   (mod 2^32)  (integer path)
+//   double cs[64]       2^eb * unit                               (integer path)
+//   double sbw[4][64]   sb as f64                                 (f64 path)
+constexpr int CR_SBQ = 0, CR_KC = 1024, CR_CS = 1280, CR_SBW = 1792, CR_BYTES = 3840;
+constexpr int SMEM_BYTES = 1024 + NSTAGE * STAGE_BYTES + NCR * CR_BYTES + 256;
+
+// NVFP4 f64-path row record, one per (row, group).
 struct __align__(16) RowScaleNv {
-  float ma;        // signed E4M3 significand (0..15), 0 for NaN
-  uint32_t hi;     // exponent word: 2^(sxa + 50) with the low 20 mantissa bits zero
+  float ma;        // signed E4M3 significand (0..15), 0 for NaN / zero
+  uint32_t hi;     // exponent word of 2^(sxa + 50), low 20 mantissa bits zero
   double d0;       // double{hi, MAGIC_BITS}
 };
 
+template <int FMT> struct Fmt;
+template <> struct Fmt<EMU_FMT_NVFP4> { static constexpr int GS = 16, GPB = 4; };
+template <> struct Fmt<EMU_FMT_MXFP4> { static constexpr int GS = 32, GPB = 2; };
+
 // ------------------------------------------------------------------------------ pre-pass
-__global__ void unpack_fp16x2_kernel(const uint8_t* __restrict__ packed, int64_t rows, int64_t K,
-                                     __half* __restrict__ out) {
-  const int64_t n8 = rows * (K / 16);               // 8-byte chunks (16 elements)
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n8; i += (int64_t)gridDim.x * blockDim.x) {
-    const uint2 w = reinterpret_cast<const uint2*>(packed)[i];
-    const uint32_t in[2] = {w.x, w.y};
-    uint32_t o[8];
+// One thread per 16 elements.  For 32-element groups the two halves sit in adjacent lanes.
+template <int GS>
+__global__ void unpack_stats_kernel(const uint8_t* __restrict__ packed, int64_t rows, int64_t K,
+                                    __half* __restrict__ out, uint32_t* __restrict__ stats) {
+  const int64_t n8 = rows * (K / 16);
+  const int64_t G = K / GS;
+  const int64_t loop = (n8 + 31) / 32 * 32;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < loop; i += (int64_t)gridDim.x * blockDim.x) {
+    uint32_t l1 = 0, li = 0;
+    const bool live = i < n8;
+    if (live) {
+      const uint2 w = reinterpret_cast<const uint2*>(packed)[i];
+      const uint32_t in[2] = {w.x, w.y};
+      uint32_t o[8];
 #pragma unroll
-    for (int h = 0; h < 2; ++h)
+      for (int h = 0; h < 2; ++h)
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const uint32_t lo = (in[h] >> (8 * q)) & 0xFu, hi = (in[h] >> (8 * q + 4)) & 0xFu;
-        const __half a = __int2half_rn(e2m1_twice(lo)), b = __int2half_rn(e2m1_twice(hi));
-        o[4 * h + q] = (uint32_t)__half_as_ushort(a) | ((uint32_t)__half_as_ushort(b) << 16);
-      }
-    uint4* dst = reinterpret_cast<uint4*>(out) + 2 * i;
-    dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
-    dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+        for (int q = 0; q < 4; ++q) {
+          const int lo = e2m1_twice((in[h] >> (8 * q)) & 0xFu), hi = e2m1_twice((in[h] >> (8 * q + 4)) & 0xFu);
+          const uint32_t alo = (uint32_t)abs(lo), ahi = (uint32_t)abs(hi);
+          l1 += alo + ahi;
+          li = max(li, max(alo, ahi));
+          o[4 * h + q] =
+              (uint32_t)__half_as_ushort(__int2half_rn(lo)) | ((uint32_t)__half_as_ushort(__int2half_rn(hi)) << 16);
+        }
+      uint4* dst = reinterpret_cast<uint4*>(out) + 2 * i;
+      dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+      dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+    }
+    if (GS == 32) {
+      l1 += __shfl_xor_sync(0xFFFFFFFFu, l1, 1);
+      li = max(li, __shfl_xor_sync(0xFFFFFFFFu, li, 1));
+    }
+    if (live && (GS == 16 || (i & 1) == 0)) {
+      const int64_t r = i / (K / 16), c = i % (K / 16);
+      stats[r * G + c / (GS / 16)] = l1 | (li << 16);
+    }
   }
 }
 
-// NVFP4 rows: RowScaleNv[rows][G]; row_nan[rows].  MXFP4 rows: f64 2^(u-129) [rows][G].
+struct PrepTables {
+  float* rmaq;          // [M][G]    integer-path row multipliers
+  double* rrs;          // [M][nb]   integer-path row exponent base
+  void* rw;             // [M][G]    f64-path rows: RowScaleNv (NVFP4) / double sa/4 (MXFP4)
+  uint32_t* row_nan;    // [M]       NVFP4: any NaN scale in the row
+  uint8_t* rinf;        // [M][nb]   MXFP4: a 255 scale in the block
+  uint8_t* colrec;      // [nb][tiles_n][CR_BYTES]
+  uint32_t* col_nan;    // [Np]
+  uint8_t* cinf;        // [Np][nb]
+  uint32_t* ast;        // [M][G]    L1 | Linf << 16
+  uint32_t* bst;        // [N][G]
+  uint32_t* rts;        // [tiles_m][G]
+  float* rtm;           // [tiles_m][G]
+  uint8_t* rtinf;       // [tiles_m][nb]
+  uint32_t* cts;        // [tiles_n][G]
+  float* ctm;           // [tiles_n][G]
+  uint8_t* ctinf;       // [tiles_n][nb]
+  uint8_t* path;        // [tiles_m][tiles_n][nb]  1 = integer path
+};
+
+// E4M3 -> (signed significand, exponent) with value = ma * 2^sx; NaN -> ma 0.
+__device__ __forceinline__ void e4m3_split(uint32_t byte, int& ma, int& sx, bool& nan) {
+  const uint32_t e = (byte >> 3) & 0xFu, m = byte & 7u;
+  nan = (e == 15u && m == 7u);
+  ma = (e == 0u) ? (int)m : (int)(8u + m);
+  sx = (e == 0u) ? -9 : (int)e - 10;
+  if (byte & 0x80u) ma = -ma;
+  if (nan) ma = 0;
+}
+
+__device__ __forceinline__ double pow2d(int e) {   // exact 2^e for e in [-1022, 1023]
+  return __longlong_as_double((long long)(e + 1023) << 52);
+}
+
+// one thread per (row, block)
 template <int FMT>
-__global__ void row_scales_kernel(const uint8_t* __restrict__ sf, int64_t rows, int64_t G, int64_t sf_cols,
-                                  void* __restrict__ table, uint8_t* __restrict__ row_nan) {
-  for (int64_t r = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; r < rows; r += (int64_t)gridDim.x * blockDim.x) {
-    bool any_nan = false;
-    for (int64_t g = 0; g < G; ++g) {
-      const uint32_t byte = sf[swz_offset(r, g, sf_cols)];
-      if (FMT == EMU_FMT_NVFP4) {
-        const uint32_t e = (byte >> 3) & 0xFu, m = byte & 7u;
-        const bool nan = (e == 15u && m == 7u);
-        any_nan |= nan;
-        int ma = (e == 0u) ? (int)m : (int)(8u + m);
-        const int sxa = (e == 0u) ? -9 : (int)e - 10;
-        if (byte & 0x80u) ma = -ma;
-        if (nan) ma = 0;
+__global__ void row_tables_kernel(const uint8_t* __restrict__ sf, int64_t M, int64_t G, int64_t nb, int64_t sf_cols,
+                                  PrepTables t) {
+  constexpr int GPB = Fmt<FMT>::GPB;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < M * nb; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / nb, kb = i % nb;
+    uint32_t byte[GPB];
+#pragma unroll
+    for (int g = 0; g < GPB; ++g) byte[g] = sf[swz_offset(r, kb * GPB + g, sf_cols)];
+    if (FMT == EMU_FMT_NVFP4) {
+      int ma[GPB], sx[GPB];
+      bool nan[GPB], any_nan = false;
+      int base = 1 << 30;
+#pragma unroll
+      for (int g = 0; g < GPB; ++g) {
+        e4m3_split(byte[g], ma[g], sx[g], nan[g]);
+        any_nan |= nan[g];
+        if (ma[g] != 0) base = min(base, sx[g]);
+      }
+      if (base == (1 << 30)) base = 0;
+#pragma unroll
+      for (int g = 0; g < GPB; ++g) {
+        t.rmaq[r * G + kb * GPB + g] = ma[g] == 0 ? 0.0f : (float)ma[g] * (float)(1 << (sx[g] - base));
         RowScaleNv rec;
-        rec.ma = (float)ma;
-        rec.hi = (uint32_t)(sxa + 1073) << 20;
+        rec.ma = (float)ma[g];
+        rec.hi = (uint32_t)(sx[g] + 1073) << 20;
         rec.d0 = __hiloint2double((int)rec.hi, (int)MAGIC_BITS);
-        static_cast<RowScaleNv*>(table)[r * G + g] = rec;
-      } else {
-        static_cast<double*>(table)[r * G + g] = ue8m0_quarter_f64(byte);
+        static_cast<RowScaleNv*>(t.rw)[r * G + kb * GPB + g] = rec;
       }
+      t.rrs[r * nb + kb] = pow2d(base - 1);     // v = p4*ma*mb*2^(sxa+sxb-2)
+      if (any_nan) atomicOr(&t.row_nan[r], 1u);
+    } else {
+      int base = 1 << 30;
+      bool inf = false;
+#pragma unroll
+      for (int g = 0; g < GPB; ++g) {
+        if (byte[g] == 255u) inf = true;
+        else base = min(base, (int)byte[g]);
+      }
+      if (base == (1 << 30)) base = 0;
+#pragma unroll
+      for (int g = 0; g < GPB; ++g) {
+        const int d = (int)byte[g] - base;
+        t.rmaq[r * G + kb * GPB + g] =
+            (byte[g] == 255u) ? 0.0f : (d < 127 ? __int_as_float((d + 127) << 23) : __int_as_float(0x7F800000));
+        static_cast<double*>(t.rw)[r * G + kb * GPB + g] = ue8m0_quarter_f64(byte[g]);
+      }
+      t.rrs[r * nb + kb] = pow2d(base - 128);  // v = p4 * 2^(ua+ub-256)
+      t.rinf[r * nb + kb] = inf ? 1 : 0;
     }
-    if (FMT == EMU_FMT_NVFP4) row_nan[r] = any_nan ? 1 : 0;
   }
 }
 
-// Column scales transposed to [G][ncols_pad] f64: NVFP4 sb (signed, 0 for NaN), MXFP4 2^(u-127).
+// one thread per (column, block), columns padded to the tile
 template <int FMT>
-__global__ void col_scales_kernel(const uint8_t* __restrict__ sf, int64_t cols, int64_t ncols_pad, int64_t G,
-                                  int64_t sf_cols, double* __restrict__ table, uint8_t* __restrict__ col_nan) {
-  const int64_t total = G * ncols_pad;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t g = i / ncols_pad, c = i % ncols_pad;
-    double v = 0.0;
-    if (c < cols) {
-      const uint32_t byte = sf[swz_offset(c, g, sf_cols)];
-      if (FMT == EMU_FMT_NVFP4) {
-        bool nan;
-        const int32_t s512 = e4m3_times_512(byte, &nan);
-        v = (double)s512 * 0x1p-9;
-      } else {
-        v = ue8m0_quarter_f64(byte) * 4.0;
-      }
+__global__ void col_tables_kernel(const uint8_t* __restrict__ sf, int64_t N, int64_t Np, int64_t G, int64_t nb,
+                                  int64_t sf_cols, PrepTables t) {
+  constexpr int GPB = Fmt<FMT>::GPB;
+  const int64_t tiles_n = Np / BN;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < Np * nb; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t kb = i / Np, n = i % Np;
+    const int64_t tn = n / BN, c = n % BN;
+    uint8_t* rec = t.colrec + (kb * tiles_n + tn) * CR_BYTES;
+    int32_t* sbq = reinterpret_cast<int32_t*>(rec + CR_SBQ);
+    uint32_t* kc = reinterpret_cast<uint32_t*>(rec + CR_KC);
+    double* cs = reinterpret_cast<double*>(rec + CR_CS);
+    double* sbw = reinterpret_cast<double*>(rec + CR_SBW);
+    uint32_t sum = 0;
+    if (n >= N) {
+#pragma unroll
+      for (int g = 0; g < GPB; ++g) { sbq[g * BN + c] = 0; sbw[g * BN + c] = 0.0; }
+      kc[c] = 0x80000000u;
+      cs[c] = 0.0;
+      t.cinf[n * nb + kb] = 0;
+      continue;
     }
-    table[i] = v;
+    uint32_t byte[GPB];
+#pragma unroll
+    for (int g = 0; g < GPB; ++g) byte[g] = sf[swz_offset(n, kb * GPB + g, sf_cols)];
+    if (FMT == EMU_FMT_NVFP4) {
+      int mb[GPB], sx[GPB];
+      bool nan[GPB], any_nan = false;
+      int base = 1 << 30;
+#pragma unroll
+      for (int g = 0; g < GPB; ++g) {
+        e4m3_split(byte[g], mb[g], sx[g], nan[g]);
+        any_nan |= nan[g];
+        if (mb[g] != 0) base = min(base, sx[g]);
+      }
+      if (base == (1 << 30)) base = 0;
+#pragma unroll
+      for (int g = 0; g < GPB; ++g) {
+        const int32_t q = mb[g] == 0 ? 0 : mb[g] * (1 << (sx[g] - base));
+        sbq[g * BN + c] = q;
+        sum += (uint32_t)q;
+        sbw[g * BN + c] = (double)mb[g] * pow2d(sx[g]);
+      }
+      cs[c] = pow2d(base - 1);
+      if (any_nan) atomicOr(&t.col_nan[n], 1u);
+      t.cinf[n * nb + kb] = 0;
+    } else {
+      int base = 1 << 30;
+      bool inf = false;
+#pragma unroll
+      for (int g = 0; g < GPB; ++g) {
+        if (byte[g] == 255u) inf = true;
+        else base = min(base, (int)byte[g]);
+      }
+      if (base == (1 << 30)) base = 0;
+#pragma unroll
+      for (int g = 0; g < GPB; ++g) {
+        const int d = (int)byte[g] - base;
+        // exponent spreads beyond 2^30 cannot pass the integer-path bounds: record a value that fails them
+        const int32_t q = (byte[g] == 255u) ? 0 : (d <= 30 ? (1 << d) : 0x7FFFFFFF);
+        sbq[g * BN + c] = q;
+        sum += (uint32_t)q;
+        sbw[g * BN + c] = ue8m0_quarter_f64(byte[g]) * 4.0;
+      }
+      cs[c] = pow2d(base - 128);
+      t.cinf[n * nb + kb] = inf ? 1 : 0;
+    }
+    kc[c] = 0x80000000u - MAGIC_BITS * sum;
   }
-  if (FMT == EMU_FMT_NVFP4) {
-    for (int64_t c = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; c < cols; c += (int64_t)gridDim.x * blockDim.x) {
-      bool any = false;
-      for (int64_t g = 0; g < G; ++g) {
-        bool nan;
-        (void)e4m3_times_512(sf[swz_offset(c, g, sf_cols)], &nan);
-        any |= nan;
+}
+
+// per (tile, group) maxima over the tile's rows (A) or columns (B); per (tile, block) inf flags
+template <int FMT>
+__global__ void tile_stats_kernel(int64_t rows, int64_t tile, int64_t ntiles, int64_t G, int64_t nb, int is_col,
+                                  PrepTables t) {
+  constexpr int GPB = Fmt<FMT>::GPB;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < ntiles * G; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t tl = i / G, g = i % G;
+    const int64_t kb = g / GPB;
+    const int64_t r0 = tl * tile, r1 = min(rows, r0 + tile);
+    uint32_t l1 = 0, li = 0;
+    float mm = 0.0f;
+    bool inf = false;
+    for (int64_t r = r0; r < r1; ++r) {
+      const uint32_t s = (is_col ? t.bst : t.ast)[r * G + g];
+      l1 = max(l1, s & 0xFFFFu);
+      li = max(li, s >> 16);
+      if (is_col) {
+        const uint8_t* rec = t.colrec + (kb * ntiles + tl) * CR_BYTES;
+        const int32_t q = reinterpret_cast<const int32_t*>(rec + CR_SBQ)[(g % GPB) * BN + (r - r0)];
+        mm = fmaxf(mm, fabsf((float)q));
+        inf |= t.cinf[r * nb + kb] != 0;
+      } else {
+        mm = fmaxf(mm, fabsf(t.rmaq[r * G + g]));
+        if (FMT == EMU_FMT_MXFP4) inf |= t.rinf[r * nb + kb] != 0;
       }
-      col_nan[c] = any ? 1 : 0;
     }
+    (is_col ? t.cts : t.rts)[tl * G + g] = l1 | (li << 16);
+    (is_col ? t.ctm : t.rtm)[tl * G + g] = mm;
+    if (g % GPB == 0) (is_col ? t.ctinf : t.rtinf)[tl * nb + kb] = inf ? 1 : 0;
+  }
+}
+
+// per (row tile, column tile, block): 1 when the integer path is exact for every output of the block
+template <int FMT>
+__global__ void decide_kernel(int64_t tiles_m, int64_t tiles_n, int64_t nb, int64_t G, PrepTables t) {
+  constexpr int GPB = Fmt<FMT>::GPB;
+  const int64_t total = tiles_m * tiles_n * nb;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t kb = i % nb, tn = (i / nb) % tiles_n, tm = i / (nb * tiles_n);
+    bool ok = !t.rtinf[tm * nb + kb] && !t.ctinf[tn * nb + kb];
+    double tsum = 0.0;
+#pragma unroll
+    for (int g = 0; g < GPB; ++g) {
+      const int64_t gg = kb * GPB + g;
+      const uint32_t ra = t.rts[tm * G + gg], cb = t.cts[tn * G + gg];
+      const double p = fmin((double)(ra & 0xFFFFu) * (double)(cb >> 16), (double)(ra >> 16) * (double)(cb & 0xFFFFu));
+      const double tmax = p * (double)t.rtm[tm * G + gg];
+      ok = ok && (p < 2048.0) && (tmax < 4194304.0);
+      tsum += tmax * (double)t.ctm[tn * G + gg];
+    }
+    ok = ok && (tsum < 2147483648.0);
+    t.path[i] = ok ? 1 : 0;
   }
 }
 
@@ -149,10 +340,14 @@ __global__ void col_scales_kernel(const uint8_t* __restrict__ sf, int64_t cols, 
 struct Params {
   int64_t M, N, K;
   int64_t G, nb, tiles_m, tiles_n;
-  const void* row_tab;        // RowScaleNv[M][G] or double[M][G]
-  const uint8_t* row_nan;     // NVFP4 only
-  const uint8_t* col_nan;     // NVFP4 only
-  const float* alpha;         // nullable
+  const float* rmaq;
+  const double* rrs;
+  const void* rw;
+  const uint32_t* row_nan;
+  const uint32_t* col_nan;
+  const uint8_t* colrec;
+  const uint8_t* path;
+  const float* alpha;
   void* out;
   int* err;
   int r3, r4, out_mode;
@@ -169,14 +364,13 @@ __device__ __forceinline__ void tile_coords(int64_t t, const Params& p, int64_t&
   tn = idx / gm;
 }
 
-// p4 -> nearest fp16 grid value (only called when |p4| >= 2048 somewhere in the warp)
+// p4 -> nearest fp16-grid value of p = p4/4, times 4
 __device__ __forceinline__ float round_p4_f(float p4) {
   return __half2float(__float2half_rn(p4 * 0.25f)) * 4.0f;
 }
 
-// NVFP4 f32-range rounding of an f64 that holds a finite value with |x| in [2^-126, 2^128) or 0:
-// clear (RZ) or round-to-nearest-even (RNE) the 29 low mantissa bits.  Values here are multiples
-// of 2^-20 below 2^64, so they are always in that range.
+// f64 holding a finite value with |x| in [2^-126, 2^128) or 0 -> the same rounded to 24 significant
+// bits (RZ: clear, RNE: round-half-even on the 29 dropped bits): exact f32 rounding in that range.
 __device__ __forceinline__ double round24(double x, int mode) {
   long long b = __double_as_longlong(x);
   if (mode == EMU_RNE) b += 0x0FFFFFFFll + ((b >> 29) & 1ll);
@@ -184,27 +378,36 @@ __device__ __forceinline__ double round24(double x, int mode) {
   return __longlong_as_double(b);
 }
 
-template <int FMT>
-__global__ void __launch_bounds__(NUM_THREADS, 1)
-emul_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                    const __grid_constant__ CUtensorMap tmSB, const Params p) {
-  constexpr int GPB = (FMT == EMU_FMT_NVFP4) ? 4 : 2;       // groups per 64-element K block
+// general f64 -> f32 rounding kept in f64: bit path in the f32 normal range, cvt otherwise
+__device__ __forceinline__ double round_to_f32_in_f64(double x, int mode) {
+  const uint32_t e = ((uint32_t)__double2hiint(x) >> 20) & 0x7FFu;
+  if ((e - 897u) < 254u || x == 0.0) return round24(x, mode);
+  return (double)round_f64_to_f32(x, mode);
+}
+
+// EPI epilogue warps (8 or 16): each thread owns one row and CPT = 64 / (EPI / 4) columns.
+template <int FMT, int EPI>
+__global__ void __launch_bounds__(32 * (2 + EPI), 1)
+emul_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const Params p) {
+  constexpr int NUM_EPI_WARPS = EPI;
+  constexpr int CPT = BN / (EPI / 4);                         // columns per epilogue thread
+  constexpr int GPB = Fmt<FMT>::GPB;
   constexpr int SET_COLS = GPB * BN;                         // TMEM columns per K block
   constexpr int NSETS = 512 / SET_COLS;                      // 2 (NVFP4) or 4 (MXFP4)
-  constexpr uint32_t SB_TX = GPB * BN * 8;
+  constexpr uint32_t CR_TX = (FMT == EMU_FMT_NVFP4) ? CR_BYTES : (uint32_t)(CR_SBW + 2 * BN * 8);
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   uint8_t* stage_base = smem;
-  double* sb_ring = reinterpret_cast<double*>(smem + NSTAGE * STAGE_BYTES);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + NSTAGE * STAGE_BYTES + NSB * SB_BYTES);
+  uint8_t* cr_ring = smem + NSTAGE * STAGE_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(cr_ring + NCR * CR_BYTES);
   uint64_t* full = bars;                       // [NSTAGE]
   uint64_t* empty = full + NSTAGE;             // [NSTAGE]
-  uint64_t* sb_full = empty + NSTAGE;          // [NSB]
-  uint64_t* sb_empty = sb_full + NSB;          // [NSB]
-  uint64_t* tm_full = sb_empty + NSB;          // [NSETS]
+  uint64_t* cr_full = empty + NSTAGE;          // [NCR]
+  uint64_t* cr_empty = cr_full + NCR;          // [NCR]
+  uint64_t* tm_full = cr_empty + NCR;          // [NSETS]
   uint64_t* tm_empty = tm_full + 4;            // [NSETS]
-  uint64_t* drain = tm_empty + 4;              // MMA completion before TMEM release
+  uint64_t* drain = tm_empty + 4;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -212,13 +415,12 @@ emul_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < NSTAGE; ++i) { ptx::mbar_init(&full[i], 1); ptx::mbar_init(&empty[i], 1); }
-    for (int i = 0; i < NSB; ++i) { ptx::mbar_init(&sb_full[i], 1); ptx::mbar_init(&sb_empty[i], 8); }
-    for (int i = 0; i < NSETS; ++i) { ptx::mbar_init(&tm_full[i], 1); ptx::mbar_init(&tm_empty[i], 8); }
+    for (int i = 0; i < NCR; ++i) { ptx::mbar_init(&cr_full[i], 1); ptx::mbar_init(&cr_empty[i], NUM_EPI_WARPS); }
+    for (int i = 0; i < NSETS; ++i) { ptx::mbar_init(&tm_full[i], 1); ptx::mbar_init(&tm_empty[i], NUM_EPI_WARPS); }
     ptx::mbar_init(drain, 1);
     ptx::fence_mbar_init();
     ptx::prefetch_tmap(&tmA);
     ptx::prefetch_tmap(&tmB);
-    ptx::prefetch_tmap(&tmSB);
   }
   if (warp == 1) {
     ptx::tmem_alloc(tmem_slot, 512);
@@ -230,7 +432,7 @@ emul_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
   const uint32_t tmem_base = *tmem_slot;
 
   if (warp == 0) {
-    // ---------------------------------------------------------------- TMA producer
+    // ---------------------------------------------------------------- producer
     if (lane == 0) {
       int64_t it = 0;
       bool ok = true;
@@ -239,26 +441,24 @@ emul_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
         tile_coords(t, p, tm, tn);
         for (int64_t kb = 0; kb < p.nb && ok; ++kb, ++it) {
           const int s = (int)(it % NSTAGE);
-          const uint32_t ph = (uint32_t)((it / NSTAGE) & 1);
-          ok = ptx::mbar_wait(&empty[s], ph ^ 1u, p.err, 1);
+          ok = ptx::mbar_wait(&empty[s], (uint32_t)((it / NSTAGE) & 1) ^ 1u, p.err, 1);
           if (!ok) break;
           uint8_t* sa = stage_base + s * STAGE_BYTES;
           ptx::mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
           ptx::tma_load_2d(sa, &tmA, &full[s], (int)(kb * BK), (int)(tm * BM));
           ptx::tma_load_2d(sa + A_BYTES, &tmB, &full[s], (int)(kb * BK), (int)(tn * BN));
-          const int q = (int)(it % NSB);
-          const uint32_t qph = (uint32_t)((it / NSB) & 1);
-          ok = ptx::mbar_wait(&sb_empty[q], qph ^ 1u, p.err, 2);
+          const int q = (int)(it % NCR);
+          ok = ptx::mbar_wait(&cr_empty[q], (uint32_t)((it / NCR) & 1) ^ 1u, p.err, 2);
           if (!ok) break;
-          ptx::mbar_arrive_expect_tx(&sb_full[q], SB_TX);
-          ptx::tma_load_2d(sb_ring + q * (SB_BYTES / 8), &tmSB, &sb_full[q], (int)(tn * BN), (int)(kb * GPB));
+          ptx::mbar_arrive_expect_tx(&cr_full[q], CR_TX);
+          ptx::bulk_load(cr_ring + q * CR_BYTES, p.colrec + (kb * p.tiles_n + tn) * CR_BYTES, CR_TX, &cr_full[q]);
         }
       }
-      // drain: every issued TMA copy must have landed before the CTA may exit (bounded waits)
+      // drain: every issued copy must have landed before the CTA may exit (bounded waits)
       for (int64_t j = (it > NSTAGE ? it - NSTAGE : 0); j < it; ++j)
         ptx::mbar_wait(&full[j % NSTAGE], (uint32_t)((j / NSTAGE) & 1), p.err, 7);
-      for (int64_t j = (it > NSB ? it - NSB : 0); j < it; ++j)
-        ptx::mbar_wait(&sb_full[j % NSB], (uint32_t)((j / NSB) & 1), p.err, 8);
+      for (int64_t j = (it > NCR ? it - NCR : 0); j < it; ++j)
+        ptx::mbar_wait(&cr_full[j % NCR], (uint32_t)((j / NCR) & 1), p.err, 8);
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
@@ -269,12 +469,10 @@ emul_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
       for (int64_t t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
         for (int64_t kb = 0; kb < p.nb && ok; ++kb, ++it) {
           const int s = (int)(it % NSTAGE);
-          const uint32_t ph = (uint32_t)((it / NSTAGE) & 1);
           const int set = (int)(it % NSETS);
-          const uint32_t tph = (uint32_t)((it / NSETS) & 1);
-          ok = ptx::mbar_wait(&tm_empty[set], tph ^ 1u, p.err, 3);
+          ok = ptx::mbar_wait(&tm_empty[set], (uint32_t)((it / NSETS) & 1) ^ 1u, p.err, 3);
           if (!ok) break;
-          ok = ptx::mbar_wait(&full[s], ph, p.err, 4);
+          ok = ptx::mbar_wait(&full[s], (uint32_t)((it / NSTAGE) & 1), p.err, 4);
           if (!ok) break;
           ptx::tc_fence_after();
           const uint32_t a_addr = ptx::smem_u32(stage_base + s * STAGE_BYTES);
@@ -284,7 +482,7 @@ emul_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
           for (int g = 0; g < GPB; ++g) {
             const uint32_t d = d_col + (uint32_t)(g * BN);
             if (FMT == EMU_FMT_NVFP4) {
-              // group g = K elements [16g, 16g+16) = bytes [32g, 32g+32) of each 128-byte row
+              // group g: K elements [16g, 16g+16) = bytes [32g, 32g+32) of each 128-byte row
               ptx::mma_f16(d, ptx::smem_desc_sw128(a_addr + 32 * g), ptx::smem_desc_sw128(b_addr + 32 * g), IDESC, 0);
             } else {
               ptx::mma_f16(d, ptx::smem_desc_sw128(a_addr + 64 * g), ptx::smem_desc_sw128(b_addr + 64 * g), IDESC, 0);
@@ -301,11 +499,12 @@ emul_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
       ptx::mbar_wait(drain, 0, p.err, 9);
     }
   } else {
-    // ---------------------------------------------------------------- epilogue (warps 2..9)
-    const int ew = warp - 2;                 // 0..7
+    // ---------------------------------------------------------------- epilogue (warps 2..17)
+    const int ew = warp - 2;                 // 0..15
     const int quarter = warp & 3;            // TMEM lane quarter this warp may access
-    const int half = ew >> 2;                // column half: 0 -> 0..31, 1 -> 32..63
+    const int col0 = (ew >> 2) * CPT;        // CPT columns of the 64-column tile
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+    const int rmode = p.nb == 1 ? p.r3 : p.r4;
     int64_t it = 0;
     bool ok = true;
     for (int64_t t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
@@ -314,92 +513,127 @@ emul_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
       const int64_t m = tm * BM + quarter * 32 + lane;
       const bool row_ok = m < p.M;
       const int64_t mr = row_ok ? m : (p.M - 1);
-      double acc[32];
+      double acc[CPT];
 #pragma unroll
-      for (int j = 0; j < 32; ++j) acc[j] = 0.0;
+      for (int j = 0; j < CPT; ++j) acc[j] = 0.0;
 
       for (int64_t kb = 0; kb < p.nb && ok; ++kb, ++it) {
         const int set = (int)(it % NSETS);
-        const uint32_t tph = (uint32_t)((it / NSETS) & 1);
-        const int q = (int)(it % NSB);
-        const uint32_t qph = (uint32_t)((it / NSB) & 1);
-        // per-row scale constants for this block's groups
-        float ma[GPB];
-        uint32_t hi[GPB];
-        double d0[GPB], sa[GPB];
-        if (FMT == EMU_FMT_NVFP4) {
-          const RowScaleNv* rs = static_cast<const RowScaleNv*>(p.row_tab) + mr * p.G + kb * GPB;
+        const int q = (int)(it % NCR);
+        const bool ipath = p.path[(tm * p.tiles_n + tn) * p.nb + kb] != 0;
+        // integer-path row constants of this block (f64-path constants are read inside that branch)
+        float mq[GPB];
+        double rs = 0.0;
+        if (ipath) {
 #pragma unroll
-          for (int g = 0; g < GPB; ++g) { const RowScaleNv r = rs[g]; ma[g] = r.ma; hi[g] = r.hi; d0[g] = r.d0; }
-        } else {
-          const double* rs = static_cast<const double*>(p.row_tab) + mr * p.G + kb * GPB;
-#pragma unroll
-          for (int g = 0; g < GPB; ++g) sa[g] = rs[g];
+          for (int g = 0; g < GPB; ++g) mq[g] = p.rmaq[mr * p.G + kb * GPB + g];
+          rs = p.rrs[mr * p.nb + kb];
         }
-        ok = __all_sync(0xFFFFFFFFu, ptx::mbar_wait(&tm_full[set], tph, p.err, 5));
+        ok = __all_sync(0xFFFFFFFFu, ptx::mbar_wait(&tm_full[set], (uint32_t)((it / NSETS) & 1), p.err, 5));
         if (!ok) break;
-        ok = __all_sync(0xFFFFFFFFu, ptx::mbar_wait(&sb_full[q], qph, p.err, 6));
+        ok = __all_sync(0xFFFFFFFFu, ptx::mbar_wait(&cr_full[q], (uint32_t)((it / NCR) & 1), p.err, 6));
         if (!ok) break;
         ptx::tc_fence_after();
-        const double* sbs = sb_ring + q * (SB_BYTES / 8);
+        const uint8_t* cr = cr_ring + q * CR_BYTES;
+        const int32_t* sbq = reinterpret_cast<const int32_t*>(cr + CR_SBQ);
+        const uint32_t* kc = reinterpret_cast<const uint32_t*>(cr + CR_KC);
+        const double* cs = reinterpret_cast<const double*>(cr + CR_CS);
+        const double* sbw = reinterpret_cast<const double*>(cr + CR_SBW);
 
 #pragma unroll
-        for (int h16 = 0; h16 < 2; ++h16) {
-          float v[GPB][16];
+        for (int c8 = 0; c8 < CPT / 8; ++c8) {
+          float v[GPB][8];
 #pragma unroll
           for (int g = 0; g < GPB; ++g)
-            ptx::tmem_ld16(tmem_base + lane_base + (uint32_t)(set * SET_COLS + g * BN + half * 32 + h16 * 16), v[g]);
+            ptx::tmem_ld8(tmem_base + lane_base + (uint32_t)(set * SET_COLS + g * BN + col0 + c8 * 8), v[g]);
           ptx::tmem_wait_ld();
-          if (h16 == 1) {
+          if (c8 == CPT / 8 - 1) {
             ptx::tc_fence_before();
             __syncwarp();
             if (lane == 0) ptx::mbar_arrive(&tm_empty[set]);
           }
-          // stage-1 fp16 rounding only matters for |p4| >= 2048 (|p| >= 512)
-          float mx = 0.0f;
+          if (ipath) {
 #pragma unroll
-          for (int g = 0; g < GPB; ++g)
+            for (int j4 = 0; j4 < 2; ++j4) {
+              const int cb = col0 + c8 * 8 + j4 * 4;
+              int4 sq[GPB];
 #pragma unroll
-            for (int j = 0; j < 16; ++j) mx = fmaxf(mx, fabsf(v[g][j]));
-          if (__any_sync(0xFFFFFFFFu, mx >= 2048.0f)) {
+              for (int g = 0; g < GPB; ++g) sq[g] = *reinterpret_cast<const int4*>(&sbq[g * BN + cb]);
+              const uint4 k4 = *reinterpret_cast<const uint4*>(&kc[cb]);
+              const double2 c01 = *reinterpret_cast<const double2*>(&cs[cb]);
+              const double2 c23 = *reinterpret_cast<const double2*>(&cs[cb + 2]);
+#pragma unroll
+              for (int jj = 0; jj < 4; ++jj) {
+                const int j = c8 * 8 + j4 * 4 + jj;
+                int s32 = 0;
+#pragma unroll
+                for (int g = 0; g < GPB; ++g) {
+                  const int qv = jj == 0 ? sq[g].x : jj == 1 ? sq[g].y : jj == 2 ? sq[g].z : sq[g].w;
+                  const float bits = __fmaf_rn(v[g][j4 * 4 + jj], mq[g], MAGIC_F);
+                  s32 += __float_as_int(bits) * qv;
+                }
+                const uint32_t kv = jj == 0 ? k4.x : jj == 1 ? k4.y : jj == 2 ? k4.z : k4.w;
+                const double cv = jj == 0 ? c01.x : jj == 1 ? c01.y : jj == 2 ? c23.x : c23.y;
+                const double tf = __dadd_rn(__hiloint2double(0x43300000, (int)((uint32_t)s32 + kv)),
+                                            -(TWO52 + 2147483648.0));
+                const double x = __fma_rn(tf, __dmul_rn(rs, cv), acc[j]);
+                acc[j] = (FMT == EMU_FMT_NVFP4) ? round24(x, rmode) : round_to_f32_in_f64(x, rmode);
+              }
+            }
+          } else {
+            float wma[GPB];
+            uint32_t whi[GPB];
+            double wd0[GPB], wsa[GPB];
+            if (FMT == EMU_FMT_NVFP4) {
+              const RowScaleNv* rw = static_cast<const RowScaleNv*>(p.rw) + mr * p.G + kb * GPB;
+#pragma unroll
+              for (int g = 0; g < GPB; ++g) { const RowScaleNv r = rw[g]; wma[g] = r.ma; whi[g] = r.hi; wd0[g] = r.d0; }
+            } else {
+              const double* rw = static_cast<const double*>(p.rw) + mr * p.G + kb * GPB;
+#pragma unroll
+              for (int g = 0; g < GPB; ++g) wsa[g] = rw[g];
+            }
+            float mx = 0.0f;
 #pragma unroll
             for (int g = 0; g < GPB; ++g)
 #pragma unroll
-              for (int j = 0; j < 16; ++j) v[g][j] = round_p4_f(v[g][j]);
-          }
+              for (int j = 0; j < 8; ++j) mx = fmaxf(mx, fabsf(v[g][j]));
+            if (__any_sync(0xFFFFFFFFu, mx >= 2048.0f)) {
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const int col = half * 32 + h16 * 16 + j;
-            double S = 0.0;
+              for (int g = 0; g < GPB; ++g)
 #pragma unroll
-            for (int g = 0; g < GPB; ++g) {
-              const double sb = sbs[g * BN + col];
-              if (FMT == EMU_FMT_NVFP4) {
-                const float bits = __fmaf_rn(v[g][j], ma[g], MAGIC_F);
-                const double dd = __hiloint2double((int)hi[g], __float_as_int(bits));
-                const double diff = __dadd_rn(dd, -d0[g]);
-                S = __fma_rn(diff, sb, S);
-              } else {
-                const float bits = __fadd_rn(v[g][j], MAGIC_F);
-                const double dd = __hiloint2double(0x43300000, __float_as_int(bits));
-                const double p4 = __dadd_rn(dd, -(4503599627370496.0 + (double)MAGIC_BITS));
-                S = __fma_rn(__dmul_rn(p4, sa[g]), sb, S);
-              }
+                for (int j = 0; j < 8; ++j) v[g][j] = round_p4_f(v[g][j]);
             }
-            const int jj = h16 * 16 + j;
-            if (FMT == EMU_FMT_NVFP4) {
-              if (p.nb == 1) acc[jj] = round24(S, p.r3);
-              else acc[jj] = round24(kb == 0 ? S : __dadd_rn(acc[jj], S), p.r4);
-            } else {
-              float a;
-              if (p.nb == 1) a = round_f64_to_f32(S, p.r3);
-              else a = round_f64_to_f32(kb == 0 ? S : __dadd_rn(acc[jj], S), p.r4);
-              acc[jj] = (double)a;
+#pragma unroll
+            for (int jj = 0; jj < 8; ++jj) {
+              const int col = col0 + c8 * 8 + jj;
+              double S = 0.0;
+#pragma unroll
+              for (int g = 0; g < GPB; ++g) {
+                const double sb = sbw[g * BN + col];
+                if (FMT == EMU_FMT_NVFP4) {
+                  const float bits = __fmaf_rn(v[g][jj], wma[g], MAGIC_F);
+                  const double diff = __dadd_rn(__hiloint2double((int)whi[g], __float_as_int(bits)), -wd0[g]);
+                  S = __fma_rn(diff, sb, S);
+                } else {
+                  const float bits = __fadd_rn(v[g][jj], MAGIC_F);
+                  const double p4 = __dadd_rn(__hiloint2double(0x43300000, __float_as_int(bits)),
+                                              -(TWO52 + (double)MAGIC_BITS));
+                  S = __fma_rn(__dmul_rn(p4, wsa[g]), sb, S);
+                }
+              }
+              const int j = c8 * 8 + jj;
+              if (FMT == EMU_FMT_NVFP4) {
+                acc[j] = round24(kb == 0 ? S : __dadd_rn(acc[j], S), rmode);
+              } else {
+                const double x = kb == 0 ? S : __dadd_rn(acc[j], S);
+                acc[j] = (double)round_f64_to_f32(x, rmode);
+              }
             }
           }
         }
         __syncwarp();
-        if (lane == 0) ptx::mbar_arrive(&sb_empty[q]);
+        if (lane == 0) ptx::mbar_arrive(&cr_empty[q]);
       }
       if (!ok) break;
       // ---- output
@@ -407,8 +641,8 @@ emul_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
         const float al = p.alpha ? *p.alpha : 1.0f;
         const bool rnan = (FMT == EMU_FMT_NVFP4) && p.row_nan[m];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const int64_t n = tn * BN + half * 32 + j;
+        for (int j = 0; j < CPT; ++j) {
+          const int64_t n = tn * BN + col0 + j;
           if (n < p.N) {
             float y = (float)acc[j];
             if (p.alpha) y = __fmul_rn(y, al);
@@ -460,22 +694,39 @@ static bool make_map_2d(CUtensorMap* m, CUtensorMapDataType dt, void* base, uint
 static size_t align_up(size_t x) { return (x + 1023) & ~(size_t)1023; }
 
 struct WsLayout {
-  size_t a16, b16, row_tab, sb_tab, row_nan, col_nan, err, total;
+  size_t a16, b16, rmaq, rrs, rw, row_nan, rinf, colrec, col_nan, cinf, ast, bst, rts, rtm, rtinf, cts, ctm, ctinf,
+      path, err, zero_begin, zero_end, total;
 };
 
 static WsLayout layout(int fmt, int64_t M, int64_t N, int64_t K) {
   const int gs = fmt == EMU_FMT_NVFP4 ? 16 : 32;
-  const int64_t G = K / gs;
-  const int64_t Np = (N + BN - 1) / BN * BN;
+  const int64_t G = K / gs, nb = K / BK;
+  const int64_t Np = (N + BN - 1) / BN * BN, tiles_n = Np / BN, tiles_m = (M + BM - 1) / BM;
   WsLayout L{};
   size_t off = 0;
-  L.a16 = off; off = align_up(off + (size_t)M * K * 2);
-  L.b16 = off; off = align_up(off + (size_t)N * K * 2);
-  L.row_tab = off; off = align_up(off + (size_t)M * G * (fmt == EMU_FMT_NVFP4 ? sizeof(RowScaleNv) : 8));
-  L.sb_tab = off; off = align_up(off + (size_t)G * Np * 8);
-  L.row_nan = off; off = align_up(off + (size_t)M);
-  L.col_nan = off; off = align_up(off + (size_t)N);
-  L.err = off; off = align_up(off + 16);
+  auto take = [&](size_t bytes) { size_t o = off; off = align_up(off + bytes); return o; };
+  L.a16 = take((size_t)M * K * 2);
+  L.b16 = take((size_t)N * K * 2);
+  L.rmaq = take((size_t)M * G * 4);
+  L.rrs = take((size_t)M * nb * 8);
+  L.rw = take((size_t)M * G * 16);
+  L.rinf = take((size_t)M * nb);
+  L.colrec = take((size_t)nb * tiles_n * CR_BYTES);
+  L.cinf = take((size_t)Np * nb);
+  L.ast = take((size_t)M * G * 4);
+  L.bst = take((size_t)N * G * 4);
+  L.rts = take((size_t)tiles_m * G * 4);
+  L.rtm = take((size_t)tiles_m * G * 4);
+  L.rtinf = take((size_t)tiles_m * nb);
+  L.cts = take((size_t)tiles_n * G * 4);
+  L.ctm = take((size_t)tiles_n * G * 4);
+  L.ctinf = take((size_t)tiles_n * nb);
+  L.path = take((size_t)tiles_m * tiles_n * nb);
+  L.zero_begin = off;                       // regions cleared before every call
+  L.row_nan = take((size_t)M * 4);
+  L.col_nan = take((size_t)Np * 4);
+  L.err = take(16);
+  L.zero_end = off;
   L.total = off;
   return L;
 }
@@ -494,72 +745,102 @@ bool gemm_tc_supported(int fmt, int w_reduce, int64_t M, int64_t N, int64_t K) {
   return true;
 }
 
-cudaError_t launch_gemm_tc(const uint8_t* A, const uint8_t* B, const uint8_t* SA, const uint8_t* SB, int64_t M,
-                           int64_t N, int64_t K, int64_t sa_cols, int64_t sb_cols, const float* alpha,
-                           const GemmArgs& args, void* out, void* workspace, cudaStream_t stream) {
+template <int FMT>
+static cudaError_t run_tc(const uint8_t* A, const uint8_t* B, const uint8_t* SA, const uint8_t* SB, int64_t M,
+                          int64_t N, int64_t K, int64_t sa_cols, int64_t sb_cols, const float* alpha,
+                          const GemmArgs& args, void* out, void* workspace, cudaStream_t stream) {
   using namespace tc;
-  const int fmt = args.format;
-  const int gs = fmt == EMU_FMT_NVFP4 ? 16 : 32;
-  const int64_t G = K / gs;
-  const int64_t Np = (N + BN - 1) / BN * BN;
-  const WsLayout L = layout(fmt, M, N, K);
+  constexpr int GS = Fmt<FMT>::GS;
+  const int64_t G = K / GS, nb = K / BK;
+  const int64_t Np = (N + BN - 1) / BN * BN, tiles_n = Np / BN, tiles_m = (M + BM - 1) / BM;
+  const WsLayout L = layout(FMT, M, N, K);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   __half* a16 = reinterpret_cast<__half*>(ws + L.a16);
   __half* b16 = reinterpret_cast<__half*>(ws + L.b16);
-  int* err = reinterpret_cast<int*>(ws + L.err);
+
+  PrepTables T;
+  T.rmaq = reinterpret_cast<float*>(ws + L.rmaq);
+  T.rrs = reinterpret_cast<double*>(ws + L.rrs);
+  T.rw = ws + L.rw;
+  T.row_nan = reinterpret_cast<uint32_t*>(ws + L.row_nan);
+  T.rinf = ws + L.rinf;
+  T.colrec = ws + L.colrec;
+  T.col_nan = reinterpret_cast<uint32_t*>(ws + L.col_nan);
+  T.cinf = ws + L.cinf;
+  T.ast = reinterpret_cast<uint32_t*>(ws + L.ast);
+  T.bst = reinterpret_cast<uint32_t*>(ws + L.bst);
+  T.rts = reinterpret_cast<uint32_t*>(ws + L.rts);
+  T.rtm = reinterpret_cast<float*>(ws + L.rtm);
+  T.rtinf = ws + L.rtinf;
+  T.cts = reinterpret_cast<uint32_t*>(ws + L.cts);
+  T.ctm = reinterpret_cast<float*>(ws + L.ctm);
+  T.ctinf = ws + L.ctinf;
+  T.path = ws + L.path;
 
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  cudaError_t e = cudaMemsetAsync(err, 0, 16, stream);
+  cudaError_t e = cudaMemsetAsync(ws + L.zero_begin, 0, L.zero_end - L.zero_begin, stream);
   if (e != cudaSuccess) return e;
 
-  auto grid_for = [&](int64_t n) { return (unsigned)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, (int64_t)sms * 16)); };
-  unpack_fp16x2_kernel<<<grid_for(M * K / 16), 256, 0, stream>>>(A, M, K, a16);
-  unpack_fp16x2_kernel<<<grid_for(N * K / 16), 256, 0, stream>>>(B, N, K, b16);
-  if (fmt == EMU_FMT_NVFP4) {
-    row_scales_kernel<EMU_FMT_NVFP4><<<grid_for(M), 256, 0, stream>>>(SA, M, G, sa_cols, ws + L.row_tab, ws + L.row_nan);
-    col_scales_kernel<EMU_FMT_NVFP4><<<grid_for(G * Np), 256, 0, stream>>>(SB, N, Np, G, sb_cols,
-                                                                          reinterpret_cast<double*>(ws + L.sb_tab), ws + L.col_nan);
-  } else {
-    row_scales_kernel<EMU_FMT_MXFP4><<<grid_for(M), 256, 0, stream>>>(SA, M, G, sa_cols, ws + L.row_tab, nullptr);
-    col_scales_kernel<EMU_FMT_MXFP4><<<grid_for(G * Np), 256, 0, stream>>>(SB, N, Np, G, sb_cols,
-                                                                          reinterpret_cast<double*>(ws + L.sb_tab), nullptr);
-  }
+  auto grid_for = [&](int64_t n) {
+    return (unsigned)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, (int64_t)sms * 16));
+  };
+  unpack_stats_kernel<GS><<<grid_for(M * K / 16), 256, 0, stream>>>(A, M, K, a16, T.ast);
+  unpack_stats_kernel<GS><<<grid_for(N * K / 16), 256, 0, stream>>>(B, N, K, b16, T.bst);
+  row_tables_kernel<FMT><<<grid_for(M * nb), 256, 0, stream>>>(SA, M, G, nb, sa_cols, T);
+  col_tables_kernel<FMT><<<grid_for(Np * nb), 256, 0, stream>>>(SB, N, Np, G, nb, sb_cols, T);
+  tile_stats_kernel<FMT><<<grid_for(tiles_m * G), 256, 0, stream>>>(M, BM, tiles_m, G, nb, 0, T);
+  tile_stats_kernel<FMT><<<grid_for(tiles_n * G), 256, 0, stream>>>(N, BN, tiles_n, G, nb, 1, T);
+  decide_kernel<FMT><<<grid_for(tiles_m * tiles_n * nb), 256, 0, stream>>>(tiles_m, tiles_n, nb, G, T);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
 
-  CUtensorMap tmA, tmB, tmSB;
-  const int gpb = fmt == EMU_FMT_NVFP4 ? 4 : 2;
+  CUtensorMap tmA, tmB;
   if (!make_map_2d(&tmA, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a16, K, M, K * 2, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !make_map_2d(&tmB, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, b16, K, N, K * 2, BK, BN, CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !make_map_2d(&tmSB, CU_TENSOR_MAP_DATA_TYPE_FLOAT64, ws + L.sb_tab, Np, G, Np * 8, BN, gpb,
-                   CU_TENSOR_MAP_SWIZZLE_NONE))
+      !make_map_2d(&tmB, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, b16, K, N, K * 2, BK, BN, CU_TENSOR_MAP_SWIZZLE_128B))
     return cudaErrorInvalidValue;
 
   Params prm;
-  prm.M = M; prm.N = N; prm.K = K; prm.G = G; prm.nb = K / BK;
-  prm.tiles_m = (M + BM - 1) / BM; prm.tiles_n = (N + BN - 1) / BN;
-  prm.row_tab = ws + L.row_tab;
-  prm.row_nan = ws + L.row_nan;
-  prm.col_nan = ws + L.col_nan;
+  prm.M = M; prm.N = N; prm.K = K; prm.G = G; prm.nb = nb;
+  prm.tiles_m = tiles_m; prm.tiles_n = tiles_n;
+  prm.rmaq = T.rmaq;
+  prm.rrs = T.rrs;
+  prm.rw = T.rw;
+  prm.row_nan = T.row_nan;
+  prm.col_nan = T.col_nan;
+  prm.colrec = T.colrec;
+  prm.path = T.path;
   prm.alpha = alpha;
   prm.out = out;
-  prm.err = err;
+  prm.err = reinterpret_cast<int*>(ws + L.err);
   prm.r3 = args.stage3_rounding;
   prm.r4 = args.stage4_rounding;
   prm.out_mode = args.out_mode;
 
-  const int64_t tiles = prm.tiles_m * prm.tiles_n;
-  const unsigned grid = (unsigned)std::min<int64_t>(tiles, sms);
-  if (fmt == EMU_FMT_NVFP4) {
-    cudaFuncSetAttribute(emul_gemm_tc_kernel<EMU_FMT_NVFP4>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-    emul_gemm_tc_kernel<EMU_FMT_NVFP4><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(tmA, tmB, tmSB, prm);
+  const unsigned grid = (unsigned)std::min<int64_t>(tiles_m * tiles_n, sms);
+  static const int epi = [] {
+    const char* v = getenv("EMUGEN_TC_EPI_WARPS");   // tuning knob: 8 or 16 epilogue warps
+    return (v && atoi(v) == 16) ? 16 : 8;
+  }();
+  if (epi == 16) {
+    e = cudaFuncSetAttribute(emul_gemm_tc_kernel<FMT, 16>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    emul_gemm_tc_kernel<FMT, 16><<<grid, 32 * 18, SMEM_BYTES, stream>>>(tmA, tmB, prm);
   } else {
-    cudaFuncSetAttribute(emul_gemm_tc_kernel<EMU_FMT_MXFP4>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-    emul_gemm_tc_kernel<EMU_FMT_MXFP4><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(tmA, tmB, tmSB, prm);
+    e = cudaFuncSetAttribute(emul_gemm_tc_kernel<FMT, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    emul_gemm_tc_kernel<FMT, 8><<<grid, 32 * 10, SMEM_BYTES, stream>>>(tmA, tmB, prm);
   }
   return cudaGetLastError();
+}
+
+cudaError_t launch_gemm_tc(const uint8_t* A, const uint8_t* B, const uint8_t* SA, const uint8_t* SB, int64_t M,
+                           int64_t N, int64_t K, int64_t sa_cols, int64_t sb_cols, const float* alpha,
+                           const GemmArgs& args, void* out, void* workspace, cudaStream_t stream) {
+  if (args.format == EMU_FMT_NVFP4)
+    return run_tc<EMU_FMT_NVFP4>(A, B, SA, SB, M, N, K, sa_cols, sb_cols, alpha, args, out, workspace, stream);
+  return run_tc<EMU_FMT_MXFP4>(A, B, SA, SB, M, N, K, sa_cols, sb_cols, alpha, args, out, workspace, stream);
 }
 
 }  // namespace emu
