@@ -123,7 +123,7 @@ __global__ void unpack_stats_kernel(const uint8_t* __restrict__ packed, int64_t 
 
 struct PrepTables {
   float* rmaq;          // [M][G]    integer-path row multipliers
-  double* rrs;          // [M][nb]   integer-path row exponent base
+  double2* rrs;         // [M][nb]   integer-path row base: {hi word of 2^(52+e) as bits, (2^52+2^31)*2^e}
   void* rw;             // [M][G]    f64-path rows: RowScaleNv (NVFP4) / double sa/4 (MXFP4)
   uint32_t* row_nan;    // [M]       NVFP4: any NaN scale in the row
   uint8_t* rinf;        // [M][nb]   MXFP4: a 255 scale in the block
@@ -132,11 +132,11 @@ struct PrepTables {
   uint8_t* cinf;        // [Np][nb]
   uint32_t* ast;        // [M][G]    L1 | Linf << 16
   uint32_t* bst;        // [N][G]
-  uint32_t* rts;        // [tiles_m][G]
-  float* rtm;           // [tiles_m][G]
+  uint32_t* rts;        // [tiles_m][G]   max L1 | max Linf << 16 over the tile's rows
+  float2* rtm;          // [tiles_m][G]   max (L1 * |mult|), max (Linf * |mult|) over the rows
   uint8_t* rtinf;       // [tiles_m][nb]
   uint32_t* cts;        // [tiles_n][G]
-  float* ctm;           // [tiles_n][G]
+  float2* ctm;          // [tiles_n][G]
   uint8_t* ctinf;       // [tiles_n][nb]
   uint8_t* path;        // [tiles_m][tiles_n][nb]  1 = integer path
 };
@@ -153,6 +153,15 @@ __device__ __forceinline__ void e4m3_split(uint32_t byte, int& ma, int& sx, bool
 
 __device__ __forceinline__ double pow2d(int e) {   // exact 2^e for e in [-1022, 1023]
   return __longlong_as_double((long long)(e + 1023) << 52);
+}
+
+// Row base record for exponent e: x = double{hi = exponent word of 2^(52+e), lo = T + 2^31} is
+// 2^(52+e) + (T + 2^31) * 2^e, so x - (2^52 + 2^31) * 2^e = T * 2^e exactly.
+__device__ __forceinline__ double2 row_base(int e) {
+  double2 r;
+  r.x = __longlong_as_double((long long)(52 + e + 1023) << 52);   // bits; only the high word is used
+  r.y = (4503599627370496.0 + 2147483648.0) * pow2d(e);
+  return r;
 }
 
 // one thread per (row, block)
@@ -185,7 +194,7 @@ __global__ void row_tables_kernel(const uint8_t* __restrict__ sf, int64_t M, int
         rec.d0 = __hiloint2double((int)rec.hi, (int)MAGIC_BITS);
         static_cast<RowScaleNv*>(t.rw)[r * G + kb * GPB + g] = rec;
       }
-      t.rrs[r * nb + kb] = pow2d(base - 1);     // v = p4*ma*mb*2^(sxa+sxb-2)
+      t.rrs[r * nb + kb] = row_base(base - 1);     // v = p4*ma*mb*2^(sxa+sxb-2)
       if (any_nan) atomicOr(&t.row_nan[r], 1u);
     } else {
       int base = 1 << 30;
@@ -200,10 +209,11 @@ __global__ void row_tables_kernel(const uint8_t* __restrict__ sf, int64_t M, int
       for (int g = 0; g < GPB; ++g) {
         const int d = (int)byte[g] - base;
         t.rmaq[r * G + kb * GPB + g] =
-            (byte[g] == 255u) ? 0.0f : (d < 127 ? __int_as_float((d + 127) << 23) : __int_as_float(0x7F800000));
+            (byte[g] == 255u) ? 0.0f : __int_as_float((min(d, 126) + 127) << 23);   // 2^126 sentinel: finite,
+                                                                                  // fails the bounds unless the data is 0
         static_cast<double*>(t.rw)[r * G + kb * GPB + g] = ue8m0_quarter_f64(byte[g]);
       }
-      t.rrs[r * nb + kb] = pow2d(base - 128);  // v = p4 * 2^(ua+ub-256)
+      t.rrs[r * nb + kb] = row_base(base - 128);  // v = p4 * 2^(ua+ub-256)
       t.rinf[r * nb + kb] = inf ? 1 : 0;
     }
   }
@@ -281,7 +291,8 @@ __global__ void col_tables_kernel(const uint8_t* __restrict__ sf, int64_t N, int
   }
 }
 
-// per (tile, group) maxima over the tile's rows (A) or columns (B); per (tile, block) inf flags
+// per (tile, group) maxima over the tile's rows (A) or columns (B) of the norms and of norm x
+// integer multiplier; per (tile, block) inf flags
 template <int FMT>
 __global__ void tile_stats_kernel(int64_t rows, int64_t tile, int64_t ntiles, int64_t G, int64_t nb, int is_col,
                                   PrepTables t) {
@@ -291,47 +302,60 @@ __global__ void tile_stats_kernel(int64_t rows, int64_t tile, int64_t ntiles, in
     const int64_t kb = g / GPB;
     const int64_t r0 = tl * tile, r1 = min(rows, r0 + tile);
     uint32_t l1 = 0, li = 0;
-    float mm = 0.0f;
+    float m1 = 0.0f, mi = 0.0f;
     bool inf = false;
     for (int64_t r = r0; r < r1; ++r) {
       const uint32_t s = (is_col ? t.bst : t.ast)[r * G + g];
-      l1 = max(l1, s & 0xFFFFu);
-      li = max(li, s >> 16);
+      const uint32_t sl1 = s & 0xFFFFu, sli = s >> 16;
+      l1 = max(l1, sl1);
+      li = max(li, sli);
+      float mult;
       if (is_col) {
         const uint8_t* rec = t.colrec + (kb * ntiles + tl) * CR_BYTES;
-        const int32_t q = reinterpret_cast<const int32_t*>(rec + CR_SBQ)[(g % GPB) * BN + (r - r0)];
-        mm = fmaxf(mm, fabsf((float)q));
+        mult = fabsf((float)reinterpret_cast<const int32_t*>(rec + CR_SBQ)[(g % GPB) * BN + (r - r0)]);
         inf |= t.cinf[r * nb + kb] != 0;
       } else {
-        mm = fmaxf(mm, fabsf(t.rmaq[r * G + g]));
+        mult = fabsf(t.rmaq[r * G + g]);
         if (FMT == EMU_FMT_MXFP4) inf |= t.rinf[r * nb + kb] != 0;
       }
+      m1 = fmaxf(m1, (float)sl1 * mult);    // products are rounded f32 maxima of values < 2^40: the
+      mi = fmaxf(mi, (float)sli * mult);    // decide kernel compares them with a 2^-20 safety margin
     }
     (is_col ? t.cts : t.rts)[tl * G + g] = l1 | (li << 16);
-    (is_col ? t.ctm : t.rtm)[tl * G + g] = mm;
+    (is_col ? t.ctm : t.rtm)[tl * G + g] = make_float2(m1, mi);
     if (g % GPB == 0) (is_col ? t.ctinf : t.rtinf)[tl * nb + kb] = inf ? 1 : 0;
   }
 }
 
-// per (row tile, column tile, block): 1 when the integer path is exact for every output of the block
+// per (row tile, column tile, block): 1 when the integer path is exact for every output of the block.
+// With L1 / Linf the norms of the 2x values of a group, |p4| <= min(L1a*Linfb, Linfa*L1b), so
+//   (a) no stage-1 fp16 rounding:   max |p4| < 2048
+//   (b) FFMA magic exact:           max |p4 * ma'| < 2^22
+//   (c) no int32 overflow:          max |sum_g p4 * ma' * mb'| < 2^31
+// are implied by the same inequalities on tile maxima of L1, Linf, L1*|ma'|, Linf*|ma'| (rows) and
+// the column counterparts.
 template <int FMT>
 __global__ void decide_kernel(int64_t tiles_m, int64_t tiles_n, int64_t nb, int64_t G, PrepTables t) {
   constexpr int GPB = Fmt<FMT>::GPB;
+  const double margin = 1.0 + 0x1p-20;   // covers the f32 rounding of the stored maxima
   const int64_t total = tiles_m * tiles_n * nb;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t kb = i % nb, tn = (i / nb) % tiles_n, tm = i / (nb * tiles_n);
     bool ok = !t.rtinf[tm * nb + kb] && !t.ctinf[tn * nb + kb];
-    double tsum = 0.0;
+    double s1 = 0.0, s2 = 0.0;
 #pragma unroll
     for (int g = 0; g < GPB; ++g) {
       const int64_t gg = kb * GPB + g;
       const uint32_t ra = t.rts[tm * G + gg], cb = t.cts[tn * G + gg];
-      const double p = fmin((double)(ra & 0xFFFFu) * (double)(cb >> 16), (double)(ra >> 16) * (double)(cb & 0xFFFFu));
-      const double tmax = p * (double)t.rtm[tm * G + gg];
+      const double l1a = ra & 0xFFFFu, lia = ra >> 16, l1b = cb & 0xFFFFu, lib = cb >> 16;
+      const float2 am = t.rtm[tm * G + gg], bm = t.ctm[tn * G + gg];
+      const double p = fmin(l1a * lib, lia * l1b);
+      const double tmax = fmin((double)am.x * lib, (double)am.y * l1b) * margin;
       ok = ok && (p < 2048.0) && (tmax < 4194304.0);
-      tsum += tmax * (double)t.ctm[tn * G + gg];
+      s1 += (double)am.x * (double)bm.y * margin;
+      s2 += (double)am.y * (double)bm.x * margin;
     }
-    ok = ok && (tsum < 2147483648.0);
+    ok = ok && (fmin(s1, s2) < 2147483648.0);
     t.path[i] = ok ? 1 : 0;
   }
 }
@@ -341,7 +365,7 @@ struct Params {
   int64_t M, N, K;
   int64_t G, nb, tiles_m, tiles_n;
   const float* rmaq;
-  const double* rrs;
+  const double2* rrs;
   const void* rw;
   const uint32_t* row_nan;
   const uint32_t* col_nan;
@@ -371,22 +395,25 @@ __device__ __forceinline__ float round_p4_f(float p4) {
 
 // f64 holding a finite value with |x| in [2^-126, 2^128) or 0 -> the same rounded to 24 significant
 // bits (RZ: clear, RNE: round-half-even on the 29 dropped bits): exact f32 rounding in that range.
-__device__ __forceinline__ double round24(double x, int mode) {
+template <int RM>
+__device__ __forceinline__ double round24(double x) {
   long long b = __double_as_longlong(x);
-  if (mode == EMU_RNE) b += 0x0FFFFFFFll + ((b >> 29) & 1ll);
+  if (RM == EMU_RNE) b += 0x0FFFFFFFll + ((b >> 29) & 1ll);
   b &= ~0x1FFFFFFFll;
   return __longlong_as_double(b);
 }
 
 // general f64 -> f32 rounding kept in f64: bit path in the f32 normal range, cvt otherwise
-__device__ __forceinline__ double round_to_f32_in_f64(double x, int mode) {
+template <int RM>
+__device__ __forceinline__ double round_to_f32_in_f64(double x) {
   const uint32_t e = ((uint32_t)__double2hiint(x) >> 20) & 0x7FFu;
-  if ((e - 897u) < 254u || x == 0.0) return round24(x, mode);
-  return (double)round_f64_to_f32(x, mode);
+  if ((e - 897u) < 254u || x == 0.0) return round24<RM>(x);
+  return (double)round_f64_to_f32(x, RM);
 }
 
 // EPI epilogue warps (8 or 16): each thread owns one row and CPT = 64 / (EPI / 4) columns.
-template <int FMT, int EPI>
+// RM: the rounding mode in effect (stage-3 mode for a single K block, else the stage-4 mode).
+template <int FMT, int EPI, int RM>
 __global__ void __launch_bounds__(32 * (2 + EPI), 1)
 emul_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const Params p) {
   constexpr int NUM_EPI_WARPS = EPI;
@@ -504,7 +531,6 @@ emul_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
     const int quarter = warp & 3;            // TMEM lane quarter this warp may access
     const int col0 = (ew >> 2) * CPT;        // CPT columns of the 64-column tile
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
-    const int rmode = p.nb == 1 ? p.r3 : p.r4;
     int64_t it = 0;
     bool ok = true;
     for (int64_t t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
@@ -517,17 +543,28 @@ emul_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
 #pragma unroll
       for (int j = 0; j < CPT; ++j) acc[j] = 0.0;
 
+      // row constants of block kb are loaded one block ahead (global-load latency off the critical path)
+      const uint8_t* path_row = p.path + (tm * p.tiles_n + tn) * p.nb;
+      bool nx_ipath = path_row[0] != 0;
+      float nx_mq[GPB];
+      double2 nx_rs;
+#pragma unroll
+      for (int g = 0; g < GPB; ++g) nx_mq[g] = p.rmaq[mr * p.G + g];
+      nx_rs = p.rrs[mr * p.nb];
       for (int64_t kb = 0; kb < p.nb && ok; ++kb, ++it) {
         const int set = (int)(it % NSETS);
         const int q = (int)(it % NCR);
-        const bool ipath = p.path[(tm * p.tiles_n + tn) * p.nb + kb] != 0;
-        // integer-path row constants of this block (f64-path constants are read inside that branch)
+        const bool ipath = nx_ipath;
         float mq[GPB];
-        double rs = 0.0;
-        if (ipath) {
 #pragma unroll
-          for (int g = 0; g < GPB; ++g) mq[g] = p.rmaq[mr * p.G + kb * GPB + g];
-          rs = p.rrs[mr * p.nb + kb];
+        for (int g = 0; g < GPB; ++g) mq[g] = nx_mq[g];
+        const uint32_t rs_hi = (uint32_t)__double2hiint(nx_rs.x);
+        const double rs_c = nx_rs.y;
+        if (kb + 1 < p.nb) {
+          nx_ipath = path_row[kb + 1] != 0;
+#pragma unroll
+          for (int g = 0; g < GPB; ++g) nx_mq[g] = p.rmaq[mr * p.G + (kb + 1) * GPB + g];
+          nx_rs = p.rrs[mr * p.nb + kb + 1];
         }
         ok = __all_sync(0xFFFFFFFFu, ptx::mbar_wait(&tm_full[set], (uint32_t)((it / NSETS) & 1), p.err, 5));
         if (!ok) break;
@@ -574,10 +611,9 @@ emul_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                 }
                 const uint32_t kv = jj == 0 ? k4.x : jj == 1 ? k4.y : jj == 2 ? k4.z : k4.w;
                 const double cv = jj == 0 ? c01.x : jj == 1 ? c01.y : jj == 2 ? c23.x : c23.y;
-                const double tf = __dadd_rn(__hiloint2double(0x43300000, (int)((uint32_t)s32 + kv)),
-                                            -(TWO52 + 2147483648.0));
-                const double x = __fma_rn(tf, __dmul_rn(rs, cv), acc[j]);
-                acc[j] = (FMT == EMU_FMT_NVFP4) ? round24(x, rmode) : round_to_f32_in_f64(x, rmode);
+                const double tf = __dadd_rn(__hiloint2double((int)rs_hi, (int)((uint32_t)s32 + kv)), -rs_c);
+                const double x = __fma_rn(tf, cv, acc[j]);
+                acc[j] = (FMT == EMU_FMT_NVFP4) ? round24<RM>(x) : round_to_f32_in_f64<RM>(x);
               }
             }
           } else {
@@ -624,10 +660,10 @@ emul_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
               }
               const int j = c8 * 8 + jj;
               if (FMT == EMU_FMT_NVFP4) {
-                acc[j] = round24(kb == 0 ? S : __dadd_rn(acc[j], S), rmode);
+                acc[j] = round24<RM>(kb == 0 ? S : __dadd_rn(acc[j], S));
               } else {
                 const double x = kb == 0 ? S : __dadd_rn(acc[j], S);
-                acc[j] = (double)round_f64_to_f32(x, rmode);
+                acc[j] = (double)round_f64_to_f32(x, RM);
               }
             }
           }
@@ -708,7 +744,7 @@ static WsLayout layout(int fmt, int64_t M, int64_t N, int64_t K) {
   L.a16 = take((size_t)M * K * 2);
   L.b16 = take((size_t)N * K * 2);
   L.rmaq = take((size_t)M * G * 4);
-  L.rrs = take((size_t)M * nb * 8);
+  L.rrs = take((size_t)M * nb * 16);
   L.rw = take((size_t)M * G * 16);
   L.rinf = take((size_t)M * nb);
   L.colrec = take((size_t)nb * tiles_n * CR_BYTES);
@@ -716,10 +752,10 @@ static WsLayout layout(int fmt, int64_t M, int64_t N, int64_t K) {
   L.ast = take((size_t)M * G * 4);
   L.bst = take((size_t)N * G * 4);
   L.rts = take((size_t)tiles_m * G * 4);
-  L.rtm = take((size_t)tiles_m * G * 4);
+  L.rtm = take((size_t)tiles_m * G * 8);
   L.rtinf = take((size_t)tiles_m * nb);
   L.cts = take((size_t)tiles_n * G * 4);
-  L.ctm = take((size_t)tiles_n * G * 4);
+  L.ctm = take((size_t)tiles_n * G * 8);
   L.ctinf = take((size_t)tiles_n * nb);
   L.path = take((size_t)tiles_m * tiles_n * nb);
   L.zero_begin = off;                       // regions cleared before every call
@@ -760,7 +796,7 @@ static cudaError_t run_tc(const uint8_t* A, const uint8_t* B, const uint8_t* SA,
 
   PrepTables T;
   T.rmaq = reinterpret_cast<float*>(ws + L.rmaq);
-  T.rrs = reinterpret_cast<double*>(ws + L.rrs);
+  T.rrs = reinterpret_cast<double2*>(ws + L.rrs);
   T.rw = ws + L.rw;
   T.row_nan = reinterpret_cast<uint32_t*>(ws + L.row_nan);
   T.rinf = ws + L.rinf;
@@ -770,10 +806,10 @@ static cudaError_t run_tc(const uint8_t* A, const uint8_t* B, const uint8_t* SA,
   T.ast = reinterpret_cast<uint32_t*>(ws + L.ast);
   T.bst = reinterpret_cast<uint32_t*>(ws + L.bst);
   T.rts = reinterpret_cast<uint32_t*>(ws + L.rts);
-  T.rtm = reinterpret_cast<float*>(ws + L.rtm);
+  T.rtm = reinterpret_cast<float2*>(ws + L.rtm);
   T.rtinf = ws + L.rtinf;
   T.cts = reinterpret_cast<uint32_t*>(ws + L.cts);
-  T.ctm = reinterpret_cast<float*>(ws + L.ctm);
+  T.ctm = reinterpret_cast<float2*>(ws + L.ctm);
   T.ctinf = ws + L.ctinf;
   T.path = ws + L.path;
 
@@ -823,15 +859,20 @@ static cudaError_t run_tc(const uint8_t* A, const uint8_t* B, const uint8_t* SA,
     const char* v = getenv("EMUGEN_TC_EPI_WARPS");   // tuning knob: 8 or 16 epilogue warps
     return (v && atoi(v) == 16) ? 16 : 8;
   }();
-  if (epi == 16) {
-    e = cudaFuncSetAttribute(emul_gemm_tc_kernel<FMT, 16>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-    if (e != cudaSuccess) return e;
-    emul_gemm_tc_kernel<FMT, 16><<<grid, 32 * 18, SMEM_BYTES, stream>>>(tmA, tmB, prm);
-  } else {
-    e = cudaFuncSetAttribute(emul_gemm_tc_kernel<FMT, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-    if (e != cudaSuccess) return e;
-    emul_gemm_tc_kernel<FMT, 8><<<grid, 32 * 10, SMEM_BYTES, stream>>>(tmA, tmB, prm);
-  }
+  const int rm = nb == 1 ? args.stage3_rounding : args.stage4_rounding;
+  auto launch = [&](auto kern, int threads) -> cudaError_t {
+    cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    if (err != cudaSuccess) return err;
+    kern<<<grid, threads, SMEM_BYTES, stream>>>(tmA, tmB, prm);
+    return cudaSuccess;
+  };
+  if (epi == 16)
+    e = rm == EMU_RNE ? launch(emul_gemm_tc_kernel<FMT, 16, EMU_RNE>, 32 * 18)
+                      : launch(emul_gemm_tc_kernel<FMT, 16, EMU_RZ>, 32 * 18);
+  else
+    e = rm == EMU_RNE ? launch(emul_gemm_tc_kernel<FMT, 8, EMU_RNE>, 32 * 10)
+                      : launch(emul_gemm_tc_kernel<FMT, 8, EMU_RZ>, 32 * 10);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 
