@@ -14,15 +14,14 @@
 //   tile stats      per (128-row | 64-column tile, group) maxima of the norms and multipliers.
 //   decide          per (row tile, column tile, block): integer path or f64 path (below).
 //
-// Main kernel: persistent, one CTA per SM, 2 + EPI warps:
+// Main kernel: persistent, one CTA per SM, 12 warps:
 //   warp 0      producer: TMA A [128 x 64] and B [64 x 64] fp16 tiles (128-byte swizzle) into a
 //               6-stage ring; one bulk copy of the block's column record into a 4-stage ring.
 //   warp 1      TMEM owner + MMA issuer: per group one tcgen05.mma kind::f16 M128 N64 K16 (NVFP4;
 //               MXFP4 groups take two, accumulated) into its own TMEM accumulator, so TMEM holds
 //               p4 for every (row, column, group) of the block.  512 columns = a ring of K-block
 //               sets (NVFP4: 2 sets of 4 x 64; MXFP4: 4 sets of 2 x 64).
-//   warps 2..   epilogue (EPI = 8 or 16 warps): a thread owns one output row (its TMEM lane) and
-//               64 / (EPI/4) columns.
+//   warps 4-11  epilogue: a thread owns one output row (its TMEM lane) and 32 columns.
 //
 // Integer path (blocks whose tile bounds prove it exact):  per group partial
 //     bits = FFMA(p4, ma * 2^(ea_g - ea), 1.5*2^23)   integer t = p4 * ma * 2^.. in the f32 mantissa
@@ -67,7 +66,15 @@ constexpr int GROUP_M = 16;                             // tile raster: 16 M-til
 //   double cs[64]       2^eb * unit                               (integer path)
 //   double sbw[4][64]   sb as f64                                 (f64 path)
 constexpr int CR_SBQ = 0, CR_KC = 1024, CR_CS = 1280, CR_SBW = 1792, CR_BYTES = 3840;
-constexpr int SMEM_BYTES = 1024 + NSTAGE * STAGE_BYTES + NCR * CR_BYTES + 256;
+// Row record of one (K block, 128-row tile):
+//   double2 rs[128]      row base {exponent word of 2^(52+e) (high half), (2^52 + 2^31) * 2^e}
+//   float   mq[GPB][128] ma * 2^(ea_g - ea)                        (integer path)
+constexpr int RR_RS = 0, RR_MQ = 2048, RR_BYTES = 4096;
+// Constant bias tiles for the block-sum path: A row r = {3072, 0, ...}, B row n = {4096, 0, ...} in
+// the 128-byte-swizzled K-major layout, so one K=16 MMA writes 3072 * 4096 = 1.5 * 2^23 everywhere.
+constexpr int BIAS_BYTES = A_BYTES + B_BYTES;
+constexpr int SMEM_BYTES = 1024 + NSTAGE * STAGE_BYTES + BIAS_BYTES + NCR * (CR_BYTES + RR_BYTES) + 256;
+constexpr uint32_t F_TO_T31 = 0x80000000u - MAGIC_BITS;   // (T + 0x4B400000) + this = T + 2^31 (mod 2^32)
 
 // NVFP4 f64-path row record, one per (row, group).
 struct __align__(16) RowScaleNv {
@@ -123,7 +130,7 @@ __global__ void unpack_stats_kernel(const uint8_t* __restrict__ packed, int64_t 
 
 struct PrepTables {
   float* rmaq;          // [M][G]    integer-path row multipliers
-  double2* rrs;         // [M][nb]   integer-path row base: {hi word of 2^(52+e) as bits, (2^52+2^31)*2^e}
+  uint8_t* rowrec;      // [nb][tiles_m][RR_BYTES]
   void* rw;             // [M][G]    f64-path rows: RowScaleNv (NVFP4) / double sa/4 (MXFP4)
   uint32_t* row_nan;    // [M]       NVFP4: any NaN scale in the row
   uint8_t* rinf;        // [M][nb]   MXFP4: a 255 scale in the block
@@ -166,11 +173,21 @@ __device__ __forceinline__ double2 row_base(int e) {
 
 // one thread per (row, block)
 template <int FMT>
-__global__ void row_tables_kernel(const uint8_t* __restrict__ sf, int64_t M, int64_t G, int64_t nb, int64_t sf_cols,
-                                  PrepTables t) {
+__global__ void row_tables_kernel(const uint8_t* __restrict__ sf, int64_t M, int64_t Mp, int64_t G, int64_t nb,
+                                  int64_t sf_cols, PrepTables t) {
   constexpr int GPB = Fmt<FMT>::GPB;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < M * nb; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t r = i / nb, kb = i % nb;
+  const int64_t tiles_m = Mp / BM;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < Mp * nb; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t kb = i / Mp, r = i % Mp;
+    uint8_t* rec = t.rowrec + (kb * tiles_m + r / BM) * RR_BYTES;
+    double2* rs = reinterpret_cast<double2*>(rec + RR_RS) + r % BM;
+    float* mq = reinterpret_cast<float*>(rec + RR_MQ) + r % BM;
+    if (r >= M) {   // rows of the last tile beyond M: finite, discarded by the epilogue
+      *rs = row_base(0);
+#pragma unroll
+      for (int g = 0; g < GPB; ++g) mq[g * BM] = 0.0f;
+      continue;
+    }
     uint32_t byte[GPB];
 #pragma unroll
     for (int g = 0; g < GPB; ++g) byte[g] = sf[swz_offset(r, kb * GPB + g, sf_cols)];
@@ -187,14 +204,16 @@ __global__ void row_tables_kernel(const uint8_t* __restrict__ sf, int64_t M, int
       if (base == (1 << 30)) base = 0;
 #pragma unroll
       for (int g = 0; g < GPB; ++g) {
-        t.rmaq[r * G + kb * GPB + g] = ma[g] == 0 ? 0.0f : (float)ma[g] * (float)(1 << (sx[g] - base));
+        const float q = ma[g] == 0 ? 0.0f : (float)ma[g] * (float)(1 << (sx[g] - base));
+        t.rmaq[r * G + kb * GPB + g] = q;
+        mq[g * BM] = q;
         RowScaleNv rec;
         rec.ma = (float)ma[g];
         rec.hi = (uint32_t)(sx[g] + 1073) << 20;
         rec.d0 = __hiloint2double((int)rec.hi, (int)MAGIC_BITS);
         static_cast<RowScaleNv*>(t.rw)[r * G + kb * GPB + g] = rec;
       }
-      t.rrs[r * nb + kb] = row_base(base - 1);     // v = p4*ma*mb*2^(sxa+sxb-2)
+      *rs = row_base(base - 1);     // v = p4*ma*mb*2^(sxa+sxb-2)
       if (any_nan) atomicOr(&t.row_nan[r], 1u);
     } else {
       int base = 1 << 30;
@@ -208,12 +227,12 @@ __global__ void row_tables_kernel(const uint8_t* __restrict__ sf, int64_t M, int
 #pragma unroll
       for (int g = 0; g < GPB; ++g) {
         const int d = (int)byte[g] - base;
-        t.rmaq[r * G + kb * GPB + g] =
-            (byte[g] == 255u) ? 0.0f : __int_as_float((min(d, 126) + 127) << 23);   // 2^126 sentinel: finite,
-                                                                                  // fails the bounds unless the data is 0
+        const float q = (byte[g] == 255u) ? 0.0f : __int_as_float((min(d, 126) + 127) << 23);   // 2^126 sentinel:
+        t.rmaq[r * G + kb * GPB + g] = q;                            // finite, fails the bounds unless the data is 0
+        mq[g * BM] = q;
         static_cast<double*>(t.rw)[r * G + kb * GPB + g] = ue8m0_quarter_f64(byte[g]);
       }
-      t.rrs[r * nb + kb] = row_base(base - 128);  // v = p4 * 2^(ua+ub-256)
+      *rs = row_base(base - 128);  // v = p4 * 2^(ua+ub-256)
       t.rinf[r * nb + kb] = inf ? 1 : 0;
     }
   }
@@ -291,6 +310,50 @@ __global__ void col_tables_kernel(const uint8_t* __restrict__ sf, int64_t N, int
   }
 }
 
+// Block-sum path operands: the fp16 "2x" operand times its integer multiplier (ma * 2^(e_g - e) for A,
+// mb * 2^(e_g - e) for B).  Exact wherever the block passes the decide test (|product| <= 65504 and at
+// most 6 significant bits); other values are never read by that path.
+__global__ void fold_rows_kernel(const __half* __restrict__ x16, int64_t rows, int64_t K, int GS,
+                                 const float* __restrict__ mult, __half* __restrict__ out) {
+  const int64_t n8 = rows * (K / 8);
+  const int64_t G = K / GS;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n8; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / (K / 8), k0 = (i % (K / 8)) * 8;
+    const float m = mult[r * G + k0 / GS];
+    const uint4 w = reinterpret_cast<const uint4*>(x16)[i];
+    uint32_t in[4] = {w.x, w.y, w.z, w.w}, o[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&in[q]));
+      const __half2 h = __floats2half2_rn(f.x * m, f.y * m);
+      o[q] = *reinterpret_cast<const uint32_t*>(&h);
+    }
+    reinterpret_cast<uint4*>(out)[i] = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+template <int FMT>
+__global__ void fold_cols_kernel(const __half* __restrict__ x16, int64_t N, int64_t K, int64_t tiles_n,
+                                 const uint8_t* __restrict__ colrec, __half* __restrict__ out) {
+  constexpr int GS = Fmt<FMT>::GS, GPB = Fmt<FMT>::GPB;
+  const int64_t n8 = N * (K / 8);
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n8; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t n = i / (K / 8), k0 = (i % (K / 8)) * 8;
+    const int64_t g = k0 / GS, kb = g / GPB;
+    const uint8_t* rec = colrec + (kb * tiles_n + n / BN) * CR_BYTES;
+    const float m = (float)reinterpret_cast<const int32_t*>(rec + CR_SBQ)[(g % GPB) * BN + n % BN];
+    const uint4 w = reinterpret_cast<const uint4*>(x16)[i];
+    uint32_t in[4] = {w.x, w.y, w.z, w.w}, o[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&in[q]));
+      const __half2 h = __floats2half2_rn(f.x * m, f.y * m);
+      o[q] = *reinterpret_cast<const uint32_t*>(&h);
+    }
+    reinterpret_cast<uint4*>(out)[i] = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
 // per (tile, group) maxima over the tile's rows (A) or columns (B) of the norms and of norm x
 // integer multiplier; per (tile, block) inf flags
 template <int FMT>
@@ -342,6 +405,7 @@ __global__ void decide_kernel(int64_t tiles_m, int64_t tiles_n, int64_t nb, int6
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t kb = i % nb, tn = (i / nb) % tiles_n, tm = i / (nb * tiles_n);
     bool ok = !t.rtinf[tm * nb + kb] && !t.ctinf[tn * nb + kb];
+    bool fold = true;
     double s1 = 0.0, s2 = 0.0;
 #pragma unroll
     for (int g = 0; g < GPB; ++g) {
@@ -352,11 +416,17 @@ __global__ void decide_kernel(int64_t tiles_m, int64_t tiles_n, int64_t nb, int6
       const double p = fmin(l1a * lib, lia * l1b);
       const double tmax = fmin((double)am.x * lib, (double)am.y * l1b) * margin;
       ok = ok && (p < 2048.0) && (tmax < 4194304.0);
+      // block-sum path: folded operands max|2a*ma'| = max Linf*|ma'| must be an exact fp16
+      fold = fold && ((double)am.y * margin <= 65504.0) && ((double)bm.y * margin <= 65504.0);
       s1 += (double)am.x * (double)bm.y * margin;
       s2 += (double)am.y * (double)bm.x * margin;
     }
-    ok = ok && (fmin(s1, s2) < 2147483648.0);
-    t.path[i] = ok ? 1 : 0;
+    const double tb = fmin(s1, s2);
+    ok = ok && (tb < 2147483648.0);
+    // the tensor core accumulates 1.5*2^23 + T in f32: exact while every partial sum stays in
+    // (2^23, 2^24), i.e. |partial sums of T| < 2^22, which tb bounds
+    fold = ok && fold && (tb < 4194304.0);
+    t.path[i] = fold ? 2 : (ok ? 1 : 0);
   }
 }
 
@@ -364,8 +434,7 @@ __global__ void decide_kernel(int64_t tiles_m, int64_t tiles_n, int64_t nb, int6
 struct Params {
   int64_t M, N, K;
   int64_t G, nb, tiles_m, tiles_n;
-  const float* rmaq;
-  const double2* rrs;
+  const uint8_t* rowrec;
   const void* rw;
   const uint32_t* row_nan;
   const uint32_t* col_nan;
@@ -411,23 +480,32 @@ __device__ __forceinline__ double round_to_f32_in_f64(double x) {
   return (double)round_f64_to_f32(x, RM);
 }
 
-// EPI epilogue warps (8 or 16): each thread owns one row and CPT = 64 / (EPI / 4) columns.
+// 12 warps: warpgroup 0 = producer (warp 0), MMA issuer and TMEM owner (warp 1), two idle warps;
+// warpgroups 1-2 = 8 epilogue warps, each thread owning one row and 32 columns of the 64-column tile.
+// Registers are moved from warpgroup 0 to the epilogue (setmaxnreg): 128 x 56 + 256 x 224 = the
+// 384 x 168 the CTA is launched with.
 // RM: the rounding mode in effect (stage-3 mode for a single K block, else the stage-4 mode).
-template <int FMT, int EPI, int RM>
-__global__ void __launch_bounds__(32 * (2 + EPI), 1)
-emul_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const Params p) {
+constexpr int EPI = 8, NUM_WARPS = 4 + EPI, REG_LOW = 56, REG_HIGH = 224;
+static_assert(128 * REG_LOW + 32 * EPI * REG_HIGH <= 32 * NUM_WARPS * 168, "register split exceeds the launch");
+template <int FMT, int RM>
+__global__ void __launch_bounds__(32 * NUM_WARPS, 1)
+emul_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                    const __grid_constant__ CUtensorMap tmAF, const __grid_constant__ CUtensorMap tmBF, const Params p) {
   constexpr int NUM_EPI_WARPS = EPI;
   constexpr int CPT = BN / (EPI / 4);                         // columns per epilogue thread
   constexpr int GPB = Fmt<FMT>::GPB;
   constexpr int SET_COLS = GPB * BN;                         // TMEM columns per K block
   constexpr int NSETS = 512 / SET_COLS;                      // 2 (NVFP4) or 4 (MXFP4)
   constexpr uint32_t CR_TX = (FMT == EMU_FMT_NVFP4) ? CR_BYTES : (uint32_t)(CR_SBW + 2 * BN * 8);
+  constexpr uint32_t RR_TX = (uint32_t)(RR_MQ + GPB * BM * 4);
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   uint8_t* stage_base = smem;
-  uint8_t* cr_ring = smem + NSTAGE * STAGE_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(cr_ring + NCR * CR_BYTES);
+  uint8_t* bias_tile = smem + NSTAGE * STAGE_BYTES;
+  uint8_t* cr_ring = bias_tile + BIAS_BYTES;
+  uint8_t* rr_ring = cr_ring + NCR * CR_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(rr_ring + NCR * RR_BYTES);
   uint64_t* full = bars;                       // [NSTAGE]
   uint64_t* empty = full + NSTAGE;             // [NSTAGE]
   uint64_t* cr_full = empty + NSTAGE;          // [NCR]
@@ -448,86 +526,117 @@ emul_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
     ptx::fence_mbar_init();
     ptx::prefetch_tmap(&tmA);
     ptx::prefetch_tmap(&tmB);
+    ptx::prefetch_tmap(&tmAF);
+    ptx::prefetch_tmap(&tmBF);
   }
   if (warp == 1) {
     ptx::tmem_alloc(tmem_slot, 512);
     ptx::tmem_relinquish();
   }
+  // bias tiles: zero, then element k = 0 of every row (its 16-byte chunk sits at chunk index r % 8)
+  for (int i = threadIdx.x; i < BIAS_BYTES / 16; i += blockDim.x)
+    reinterpret_cast<uint4*>(bias_tile)[i] = make_uint4(0, 0, 0, 0);
+  __syncthreads();
+  for (int r = threadIdx.x; r < BM + BN; r += blockDim.x) {
+    const int rr = r < BM ? r : r - BM;
+    uint8_t* base = bias_tile + (r < BM ? 0 : A_BYTES);
+    *reinterpret_cast<uint16_t*>(base + rr * 128 + (rr & 7) * 16) = r < BM ? (uint16_t)0x6A00u   // 3072
+                                                                           : (uint16_t)0x6C00u;  // 4096
+  }
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // generic-proxy writes -> tensor core
   ptx::tc_fence_before();
   __syncthreads();
   ptx::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-
-  if (warp == 0) {
-    // ---------------------------------------------------------------- producer
-    if (lane == 0) {
-      int64_t it = 0;
-      bool ok = true;
-      for (int64_t t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
-        int64_t tm, tn;
-        tile_coords(t, p, tm, tn);
-        for (int64_t kb = 0; kb < p.nb && ok; ++kb, ++it) {
-          const int s = (int)(it % NSTAGE);
-          ok = ptx::mbar_wait(&empty[s], (uint32_t)((it / NSTAGE) & 1) ^ 1u, p.err, 1);
-          if (!ok) break;
-          uint8_t* sa = stage_base + s * STAGE_BYTES;
-          ptx::mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
-          ptx::tma_load_2d(sa, &tmA, &full[s], (int)(kb * BK), (int)(tm * BM));
-          ptx::tma_load_2d(sa + A_BYTES, &tmB, &full[s], (int)(kb * BK), (int)(tn * BN));
-          const int q = (int)(it % NCR);
-          ok = ptx::mbar_wait(&cr_empty[q], (uint32_t)((it / NCR) & 1) ^ 1u, p.err, 2);
-          if (!ok) break;
-          ptx::mbar_arrive_expect_tx(&cr_full[q], CR_TX);
-          ptx::bulk_load(cr_ring + q * CR_BYTES, p.colrec + (kb * p.tiles_n + tn) * CR_BYTES, CR_TX, &cr_full[q]);
-        }
-      }
-      // drain: every issued copy must have landed before the CTA may exit (bounded waits)
-      for (int64_t j = (it > NSTAGE ? it - NSTAGE : 0); j < it; ++j)
-        ptx::mbar_wait(&full[j % NSTAGE], (uint32_t)((j / NSTAGE) & 1), p.err, 7);
-      for (int64_t j = (it > NCR ? it - NCR : 0); j < it; ++j)
-        ptx::mbar_wait(&cr_full[j % NCR], (uint32_t)((j / NCR) & 1), p.err, 8);
-    }
-  } else if (warp == 1) {
-    // ---------------------------------------------------------------- MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t IDESC = ptx::idesc_f16_f32(BM, BN);
-      int64_t it = 0;
-      bool ok = true;
-      for (int64_t t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
-        for (int64_t kb = 0; kb < p.nb && ok; ++kb, ++it) {
-          const int s = (int)(it % NSTAGE);
-          const int set = (int)(it % NSETS);
-          ok = ptx::mbar_wait(&tm_empty[set], (uint32_t)((it / NSETS) & 1) ^ 1u, p.err, 3);
-          if (!ok) break;
-          ok = ptx::mbar_wait(&full[s], (uint32_t)((it / NSTAGE) & 1), p.err, 4);
-          if (!ok) break;
-          ptx::tc_fence_after();
-          const uint32_t a_addr = ptx::smem_u32(stage_base + s * STAGE_BYTES);
-          const uint32_t b_addr = a_addr + A_BYTES;
-          const uint32_t d_col = tmem_base + (uint32_t)(set * SET_COLS);
-#pragma unroll
-          for (int g = 0; g < GPB; ++g) {
-            const uint32_t d = d_col + (uint32_t)(g * BN);
-            if (FMT == EMU_FMT_NVFP4) {
-              // group g: K elements [16g, 16g+16) = bytes [32g, 32g+32) of each 128-byte row
-              ptx::mma_f16(d, ptx::smem_desc_sw128(a_addr + 32 * g), ptx::smem_desc_sw128(b_addr + 32 * g), IDESC, 0);
-            } else {
-              ptx::mma_f16(d, ptx::smem_desc_sw128(a_addr + 64 * g), ptx::smem_desc_sw128(b_addr + 64 * g), IDESC, 0);
-              ptx::mma_f16(d, ptx::smem_desc_sw128(a_addr + 64 * g + 32), ptx::smem_desc_sw128(b_addr + 64 * g + 32),
-                           IDESC, 1);
-            }
+  // the register limits hold for the code each call dominates, so they sit inside the role branches
+  if (warp < 4) {
+    ptx::setmaxnreg_dec<REG_LOW>();
+    if (warp == 0) {
+      // ---------------------------------------------------------------- producer
+      if (lane == 0) {
+        int64_t it = 0;
+        bool ok = true;
+        for (int64_t t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+          int64_t tm, tn;
+          tile_coords(t, p, tm, tn);
+          for (int64_t kb = 0; kb < p.nb && ok; ++kb, ++it) {
+            const int s = (int)(it % NSTAGE);
+            ok = ptx::mbar_wait(&empty[s], (uint32_t)((it / NSTAGE) & 1) ^ 1u, p.err, 1);
+            if (!ok) break;
+            uint8_t* sa = stage_base + s * STAGE_BYTES;
+            const bool fold = p.path[(tm * p.tiles_n + tn) * p.nb + kb] == 2;
+            ptx::mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
+            ptx::tma_load_2d(sa, fold ? &tmAF : &tmA, &full[s], (int)(kb * BK), (int)(tm * BM));
+            ptx::tma_load_2d(sa + A_BYTES, fold ? &tmBF : &tmB, &full[s], (int)(kb * BK), (int)(tn * BN));
+            const int q = (int)(it % NCR);
+            ok = ptx::mbar_wait(&cr_empty[q], (uint32_t)((it / NCR) & 1) ^ 1u, p.err, 2);
+            if (!ok) break;
+            ptx::mbar_arrive_expect_tx(&cr_full[q], CR_TX + RR_TX);
+            ptx::bulk_load(cr_ring + q * CR_BYTES, p.colrec + (kb * p.tiles_n + tn) * CR_BYTES, CR_TX, &cr_full[q]);
+            ptx::bulk_load(rr_ring + q * RR_BYTES, p.rowrec + (kb * p.tiles_m + tm) * RR_BYTES, RR_TX, &cr_full[q]);
           }
-          ptx::mma_commit(&empty[s]);
-          ptx::mma_commit(&tm_full[set]);
         }
+        // drain: every issued copy must have landed before the CTA may exit (bounded waits)
+        for (int64_t j = (it > NSTAGE ? it - NSTAGE : 0); j < it; ++j)
+          ptx::mbar_wait(&full[j % NSTAGE], (uint32_t)((j / NSTAGE) & 1), p.err, 7);
+        for (int64_t j = (it > NCR ? it - NCR : 0); j < it; ++j)
+          ptx::mbar_wait(&cr_full[j % NCR], (uint32_t)((j / NCR) & 1), p.err, 8);
       }
-      // drain: all issued MMAs complete before TMEM is released
-      ptx::mma_commit(drain);
-      ptx::mbar_wait(drain, 0, p.err, 9);
+    } else if (warp == 1) {
+      // ---------------------------------------------------------------- MMA issuer
+      if (lane == 0) {
+        constexpr uint32_t IDESC = ptx::idesc_f16_f32(BM, BN);
+        int64_t it = 0;
+        bool ok = true;
+        for (int64_t t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+          int64_t tm, tn;
+          tile_coords(t, p, tm, tn);
+          const uint8_t* path_row = p.path + (tm * p.tiles_n + tn) * p.nb;
+          for (int64_t kb = 0; kb < p.nb && ok; ++kb, ++it) {
+            const int s = (int)(it % NSTAGE);
+            const int set = (int)(it % NSETS);
+            const bool fold = path_row[kb] == 2;
+            ok = ptx::mbar_wait(&tm_empty[set], (uint32_t)((it / NSETS) & 1) ^ 1u, p.err, 3);
+            if (!ok) break;
+            ok = ptx::mbar_wait(&full[s], (uint32_t)((it / NSTAGE) & 1), p.err, 4);
+            if (!ok) break;
+            ptx::tc_fence_after();
+            const uint32_t a_addr = ptx::smem_u32(stage_base + s * STAGE_BYTES);
+            const uint32_t b_addr = a_addr + A_BYTES;
+            const uint32_t d_col = tmem_base + (uint32_t)(set * SET_COLS);
+            if (fold) {
+              // block sum: bias 1.5*2^23, then every group accumulated into one accumulator
+              const uint32_t ba = ptx::smem_u32(bias_tile);
+              ptx::mma_f16(d_col, ptx::smem_desc_sw128(ba), ptx::smem_desc_sw128(ba + A_BYTES), IDESC, 0);
+  #pragma unroll
+              for (int kk = 0; kk < BK / 16; ++kk)
+                ptx::mma_f16(d_col, ptx::smem_desc_sw128(a_addr + 32 * kk), ptx::smem_desc_sw128(b_addr + 32 * kk), IDESC, 1);
+            } else
+  #pragma unroll
+            for (int g = 0; g < GPB; ++g) {
+              const uint32_t d = d_col + (uint32_t)(g * BN);
+              if (FMT == EMU_FMT_NVFP4) {
+                // group g: K elements [16g, 16g+16) = bytes [32g, 32g+32) of each 128-byte row
+                ptx::mma_f16(d, ptx::smem_desc_sw128(a_addr + 32 * g), ptx::smem_desc_sw128(b_addr + 32 * g), IDESC, 0);
+              } else {
+                ptx::mma_f16(d, ptx::smem_desc_sw128(a_addr + 64 * g), ptx::smem_desc_sw128(b_addr + 64 * g), IDESC, 0);
+                ptx::mma_f16(d, ptx::smem_desc_sw128(a_addr + 64 * g + 32), ptx::smem_desc_sw128(b_addr + 64 * g + 32),
+                             IDESC, 1);
+              }
+            }
+            ptx::mma_commit(&empty[s]);
+            ptx::mma_commit(&tm_full[set]);
+          }
+        }
+        // drain: all issued MMAs complete before TMEM is released
+        ptx::mma_commit(drain);
+        ptx::mbar_wait(drain, 0, p.err, 9);
+      }
     }
   } else {
-    // ---------------------------------------------------------------- epilogue (warps 2..17)
-    const int ew = warp - 2;                 // 0..15
+    ptx::setmaxnreg_inc<REG_HIGH>();
+    // ---------------------------------------------------------------- epilogue (warps 4..11)
+    const int ew = warp - 4;                 // 0..7
     const int quarter = warp & 3;            // TMEM lane quarter this warp may access
     const int col0 = (ew >> 2) * CPT;        // CPT columns of the 64-column tile
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
@@ -543,29 +652,15 @@ emul_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
 #pragma unroll
       for (int j = 0; j < CPT; ++j) acc[j] = 0.0;
 
-      // row constants of block kb are loaded one block ahead (global-load latency off the critical path)
       const uint8_t* path_row = p.path + (tm * p.tiles_n + tn) * p.nb;
-      bool nx_ipath = path_row[0] != 0;
-      float nx_mq[GPB];
-      double2 nx_rs;
-#pragma unroll
-      for (int g = 0; g < GPB; ++g) nx_mq[g] = p.rmaq[mr * p.G + g];
-      nx_rs = p.rrs[mr * p.nb];
+      int nx_path = path_row[0];
+      const int rl = quarter * 32 + lane;      // row within the tile
       for (int64_t kb = 0; kb < p.nb && ok; ++kb, ++it) {
         const int set = (int)(it % NSETS);
         const int q = (int)(it % NCR);
-        const bool ipath = nx_ipath;
-        float mq[GPB];
-#pragma unroll
-        for (int g = 0; g < GPB; ++g) mq[g] = nx_mq[g];
-        const uint32_t rs_hi = (uint32_t)__double2hiint(nx_rs.x);
-        const double rs_c = nx_rs.y;
-        if (kb + 1 < p.nb) {
-          nx_ipath = path_row[kb + 1] != 0;
-#pragma unroll
-          for (int g = 0; g < GPB; ++g) nx_mq[g] = p.rmaq[mr * p.G + (kb + 1) * GPB + g];
-          nx_rs = p.rrs[mr * p.nb + kb + 1];
-        }
+        const int pcode = nx_path;
+        const bool ipath = pcode != 0;
+        if (kb + 1 < p.nb) nx_path = path_row[kb + 1];
         ok = __all_sync(0xFFFFFFFFu, ptx::mbar_wait(&tm_full[set], (uint32_t)((it / NSETS) & 1), p.err, 5));
         if (!ok) break;
         ok = __all_sync(0xFFFFFFFFu, ptx::mbar_wait(&cr_full[q], (uint32_t)((it / NCR) & 1), p.err, 6));
@@ -576,7 +671,40 @@ emul_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
         const uint32_t* kc = reinterpret_cast<const uint32_t*>(cr + CR_KC);
         const double* cs = reinterpret_cast<const double*>(cr + CR_CS);
         const double* sbw = reinterpret_cast<const double*>(cr + CR_SBW);
+        const uint8_t* rr = rr_ring + q * RR_BYTES;
+        const double2 rsv = reinterpret_cast<const double2*>(rr + RR_RS)[rl];
+        const uint32_t rs_hi = (uint32_t)__double2hiint(rsv.x);
+        const double rs_c = rsv.y;
 
+        if (pcode == 2) {
+          // block-sum path: one TMEM word per output, = 0x4B400000 + T
+#pragma unroll
+          for (int c8 = 0; c8 < CPT / 8; ++c8) {
+            float v[8];
+            ptx::tmem_ld8(tmem_base + lane_base + (uint32_t)(set * SET_COLS + col0 + c8 * 8), v);
+            ptx::tmem_wait_ld();
+            if (c8 == CPT / 8 - 1) {
+              ptx::tc_fence_before();
+              __syncwarp();
+              if (lane == 0) ptx::mbar_arrive(&tm_empty[set]);
+            }
+#pragma unroll
+            for (int j4 = 0; j4 < 2; ++j4) {
+              const int cb = col0 + c8 * 8 + j4 * 4;
+              const double2 c01 = *reinterpret_cast<const double2*>(&cs[cb]);
+              const double2 c23 = *reinterpret_cast<const double2*>(&cs[cb + 2]);
+#pragma unroll
+              for (int jj = 0; jj < 4; ++jj) {
+                const int j = c8 * 8 + j4 * 4 + jj;
+                const double cv = jj == 0 ? c01.x : jj == 1 ? c01.y : jj == 2 ? c23.x : c23.y;
+                const uint32_t lo = __float_as_uint(v[j4 * 4 + jj]) + F_TO_T31;
+                const double tf = __dadd_rn(__hiloint2double((int)rs_hi, (int)lo), -rs_c);
+                const double x = __fma_rn(tf, cv, acc[j]);
+                acc[j] = (FMT == EMU_FMT_NVFP4) ? round24<RM>(x) : round_to_f32_in_f64<RM>(x);
+              }
+            }
+          }
+        } else
 #pragma unroll
         for (int c8 = 0; c8 < CPT / 8; ++c8) {
           float v[GPB][8];
@@ -590,6 +718,9 @@ emul_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
             if (lane == 0) ptx::mbar_arrive(&tm_empty[set]);
           }
           if (ipath) {
+            float mq[GPB];
+#pragma unroll
+            for (int g = 0; g < GPB; ++g) mq[g] = reinterpret_cast<const float*>(rr + RR_MQ)[g * BM + rl];
 #pragma unroll
             for (int j4 = 0; j4 < 2; ++j4) {
               const int cb = col0 + c8 * 8 + j4 * 4;
@@ -730,7 +861,7 @@ static bool make_map_2d(CUtensorMap* m, CUtensorMapDataType dt, void* base, uint
 static size_t align_up(size_t x) { return (x + 1023) & ~(size_t)1023; }
 
 struct WsLayout {
-  size_t a16, b16, rmaq, rrs, rw, row_nan, rinf, colrec, col_nan, cinf, ast, bst, rts, rtm, rtinf, cts, ctm, ctinf,
+  size_t a16, b16, af16, bf16, rmaq, rowrec, rw, row_nan, rinf, colrec, col_nan, cinf, ast, bst, rts, rtm, rtinf, cts, ctm, ctinf,
       path, err, zero_begin, zero_end, total;
 };
 
@@ -743,8 +874,10 @@ static WsLayout layout(int fmt, int64_t M, int64_t N, int64_t K) {
   auto take = [&](size_t bytes) { size_t o = off; off = align_up(off + bytes); return o; };
   L.a16 = take((size_t)M * K * 2);
   L.b16 = take((size_t)N * K * 2);
+  L.af16 = take((size_t)M * K * 2);
+  L.bf16 = take((size_t)N * K * 2);
   L.rmaq = take((size_t)M * G * 4);
-  L.rrs = take((size_t)M * nb * 16);
+  L.rowrec = take((size_t)nb * tiles_m * RR_BYTES);
   L.rw = take((size_t)M * G * 16);
   L.rinf = take((size_t)M * nb);
   L.colrec = take((size_t)nb * tiles_n * CR_BYTES);
@@ -796,7 +929,7 @@ static cudaError_t run_tc(const uint8_t* A, const uint8_t* B, const uint8_t* SA,
 
   PrepTables T;
   T.rmaq = reinterpret_cast<float*>(ws + L.rmaq);
-  T.rrs = reinterpret_cast<double2*>(ws + L.rrs);
+  T.rowrec = ws + L.rowrec;
   T.rw = ws + L.rw;
   T.row_nan = reinterpret_cast<uint32_t*>(ws + L.row_nan);
   T.rinf = ws + L.rinf;
@@ -824,24 +957,29 @@ static cudaError_t run_tc(const uint8_t* A, const uint8_t* B, const uint8_t* SA,
   };
   unpack_stats_kernel<GS><<<grid_for(M * K / 16), 256, 0, stream>>>(A, M, K, a16, T.ast);
   unpack_stats_kernel<GS><<<grid_for(N * K / 16), 256, 0, stream>>>(B, N, K, b16, T.bst);
-  row_tables_kernel<FMT><<<grid_for(M * nb), 256, 0, stream>>>(SA, M, G, nb, sa_cols, T);
+  row_tables_kernel<FMT><<<grid_for(tiles_m * BM * nb), 256, 0, stream>>>(SA, M, tiles_m * BM, G, nb, sa_cols, T);
   col_tables_kernel<FMT><<<grid_for(Np * nb), 256, 0, stream>>>(SB, N, Np, G, nb, sb_cols, T);
   tile_stats_kernel<FMT><<<grid_for(tiles_m * G), 256, 0, stream>>>(M, BM, tiles_m, G, nb, 0, T);
   tile_stats_kernel<FMT><<<grid_for(tiles_n * G), 256, 0, stream>>>(N, BN, tiles_n, G, nb, 1, T);
   decide_kernel<FMT><<<grid_for(tiles_m * tiles_n * nb), 256, 0, stream>>>(tiles_m, tiles_n, nb, G, T);
+  __half* af16 = reinterpret_cast<__half*>(ws + L.af16);
+  __half* bf16 = reinterpret_cast<__half*>(ws + L.bf16);
+  fold_rows_kernel<<<grid_for(M * K / 8), 256, 0, stream>>>(a16, M, K, GS, T.rmaq, af16);
+  fold_cols_kernel<FMT><<<grid_for(N * K / 8), 256, 0, stream>>>(b16, N, K, tiles_n, T.colrec, bf16);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
 
-  CUtensorMap tmA, tmB;
+  CUtensorMap tmA, tmB, tmAF, tmBF;
   if (!make_map_2d(&tmA, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a16, K, M, K * 2, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !make_map_2d(&tmB, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, b16, K, N, K * 2, BK, BN, CU_TENSOR_MAP_SWIZZLE_128B))
+      !make_map_2d(&tmB, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, b16, K, N, K * 2, BK, BN, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !make_map_2d(&tmAF, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, af16, K, M, K * 2, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !make_map_2d(&tmBF, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, bf16, K, N, K * 2, BK, BN, CU_TENSOR_MAP_SWIZZLE_128B))
     return cudaErrorInvalidValue;
 
   Params prm;
   prm.M = M; prm.N = N; prm.K = K; prm.G = G; prm.nb = nb;
   prm.tiles_m = tiles_m; prm.tiles_n = tiles_n;
-  prm.rmaq = T.rmaq;
-  prm.rrs = T.rrs;
+  prm.rowrec = T.rowrec;
   prm.rw = T.rw;
   prm.row_nan = T.row_nan;
   prm.col_nan = T.col_nan;
@@ -855,23 +993,15 @@ static cudaError_t run_tc(const uint8_t* A, const uint8_t* B, const uint8_t* SA,
   prm.out_mode = args.out_mode;
 
   const unsigned grid = (unsigned)std::min<int64_t>(tiles_m * tiles_n, sms);
-  static const int epi = [] {
-    const char* v = getenv("EMUGEN_TC_EPI_WARPS");   // tuning knob: 8 or 16 epilogue warps
-    return (v && atoi(v) == 16) ? 16 : 8;
-  }();
   const int rm = nb == 1 ? args.stage3_rounding : args.stage4_rounding;
   auto launch = [&](auto kern, int threads) -> cudaError_t {
     cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
     if (err != cudaSuccess) return err;
-    kern<<<grid, threads, SMEM_BYTES, stream>>>(tmA, tmB, prm);
+    kern<<<grid, threads, SMEM_BYTES, stream>>>(tmA, tmB, tmAF, tmBF, prm);
     return cudaSuccess;
   };
-  if (epi == 16)
-    e = rm == EMU_RNE ? launch(emul_gemm_tc_kernel<FMT, 16, EMU_RNE>, 32 * 18)
-                      : launch(emul_gemm_tc_kernel<FMT, 16, EMU_RZ>, 32 * 18);
-  else
-    e = rm == EMU_RNE ? launch(emul_gemm_tc_kernel<FMT, 8, EMU_RNE>, 32 * 10)
-                      : launch(emul_gemm_tc_kernel<FMT, 8, EMU_RZ>, 32 * 10);
+  e = rm == EMU_RNE ? launch(emul_gemm_tc_kernel<FMT, EMU_RNE>, 32 * NUM_WARPS)
+                    : launch(emul_gemm_tc_kernel<FMT, EMU_RZ>, 32 * NUM_WARPS);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
