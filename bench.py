@@ -10,7 +10,9 @@ data, drawn on the CPU and moved to the GPU.  One step = the public path a calle
 from pinned memory and the device->host copy of the output.  Multi-GPU: every rank runs its own
 seeded case (weak scaling); timing is the max over ranks of CUDA-event time.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--mnk M,N,K]
+
+--mnk shrinks the problem for profiling captures (the headline line is taken at the default 8192^3).
 """
 from __future__ import annotations
 
@@ -49,6 +51,35 @@ def make_inputs(rank: int):
     return a.half(), b.half()
 
 
+def our_launches_per_step(step, a, b) -> int:
+    """Kernels of libemugen (names in namespace emu::) launched by one step, counted from a CUPTI
+    trace of an extra step run outside the timed region."""
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+
+    try:
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            step(a, b)
+            torch.cuda.synchronize()
+        return sum(e.count for e in prof.key_averages() if "emu::" in e.key)
+    except Exception as e:  # e.g. another CUPTI client (a profiler) holds the device
+        log(f"launch count unavailable: {type(e).__name__}: {e}")
+        return None
+
+
+def ncu_traffic():
+    """DRAM bytes (read + write) of one emul_gemm_tc_kernel launch at this workload, from the committed
+    ncu summary (a line `traffic_bytes_per_launch: N`), or None."""
+    f = REPO / "profiles" / "emul_gemm_tc_kernel.nvfp4_8192.txt"
+    try:
+        for line in f.read_text().splitlines():
+            if line.startswith("traffic_bytes_per_launch:"):
+                return int(line.split(":", 1)[1].strip())
+    except OSError:
+        pass
+    return None
+
+
 def peaks():
     p = REPO / "MEASURED_PEAKS.json"
     if p.is_file():
@@ -58,55 +89,91 @@ def peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms while the timed region runs."""
+    """SM clock, power and clock-event reasons of this process's GPU, sampled every 20 ms through NVML
+    (read-only queries) while the timed region runs; nvidia-smi at 100 ms when NVML is unavailable."""
 
-    FIELDS = "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active"
+    REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+               0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+               0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting"}
 
-    def __init__(self, index: int):
-        self.index = index
-        self.proc = None
-        self.path = Path(os.environ.get("TMPDIR", "/tmp")) / f"emugen_clocks_{os.getpid()}.csv"
+    def __init__(self, device: int):
+        self.device = device
+        self.samples = []      # (sm_mhz, reasons_bits)
+        self.max_mhz = None
+        self._stop = None
+        self._thread = None
+        self._proc = None
+
+    def _nvml_handle(self):
+        import pynvml
+        import torch
+
+        pynvml.nvmlInit()
+        pr = torch.cuda.get_device_properties(self.device)
+        bus = f"{pr.pci_domain_id:08x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+        return pynvml, pynvml.nvmlDeviceGetHandleByPciBusId(bus)
 
     def __enter__(self):
+        import threading
+
         try:
-            self.f = open(self.path, "w")
-            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                                          "-i", str(self.index), "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+            nv, h = self._nvml_handle()
+            self.max_mhz = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+            self._stop = threading.Event()
+
+            def run():
+                while not self._stop.is_set():
+                    try:
+                        self.samples.append((nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM),
+                                             nv.nvmlDeviceGetCurrentClocksEventReasons(h)))
+                    except Exception:
+                        pass
+                    self._stop.wait(0.02)
+
+            self._thread = threading.Thread(target=run, daemon=True)
+            self._thread.start()
         except Exception:
-            self.proc = None
+            self._thread = None
+            self._path = Path(os.environ.get("TMPDIR", "/tmp")) / f"emugen_clocks_{os.getpid()}.csv"
+            try:
+                self._f = open(self._path, "w")
+                self._proc = subprocess.Popen(
+                    ["nvidia-smi", "--query-gpu=clocks.sm,clocks.max.sm,clocks_event_reasons.active",
+                     "--format=csv,noheader,nounits", "-i", str(self.device), "-lms", "100"],
+                    stdout=self._f, stderr=subprocess.DEVNULL)
+            except Exception:
+                self._proc = None
         return self
 
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join(timeout=2)
+        if self._proc is not None:
+            self._proc.terminate()
             try:
-                self.proc.wait(timeout=5)
+                self._proc.wait(timeout=5)
             except Exception:
-                self.proc.kill()
-            self.f.close()
+                self._proc.kill()
+            self._f.close()
+            try:
+                for r in self._path.read_text().strip().splitlines():
+                    c = r.split(",")
+                    self.samples.append((float(c[0]), int(c[2].strip(), 16)))
+                    self.max_mhz = float(c[1])
+            except Exception:
+                pass
 
     def summary(self):
-        REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
-                   0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
-                   0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting"}
-        try:
-            rows = [r.split(",") for r in self.path.read_text().strip().splitlines() if r.strip()]
-        except Exception:
-            rows = []
-        sm, mx, reasons = [], None, set()
-        for r in rows:
-            try:
-                sm.append(float(r[1]))
-                mx = float(r[2])
-                bits = int(r[4].strip(), 16)
-                for k, v in REASONS.items():
-                    if bits & k and v != "gpu_idle":
-                        reasons.add(v)
-            except Exception:
-                continue
-        if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unsampled"], "samples": 0}
+        reasons = set()
+        for _, bits in self.samples:
+            for k, v in self.REASONS.items():
+                if bits & k and v != "gpu_idle":
+                    reasons.add(v)
+        return {"sm_mhz": statistics.median(s for s, _ in self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(reasons), "samples": len(self.samples)}
 
 
 def cpu_baseline(state_cpu, steps: int = 1):
@@ -199,7 +266,11 @@ def main() -> int:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--mnk", default=None, help="M,N,K (default 8192,8192,8192)")
     args = ap.parse_args()
+    global M, N, K
+    if args.mnk:
+        M, N, K = (int(x) for x in args.mnk.split(","))
     if args.warmup < 3:
         log("warmup raised to 3 (minimum)")
         args.warmup = 3
@@ -239,6 +310,7 @@ def main() -> int:
     for _ in range(args.warmup):
         st, out = step(a_d, b_d)
     torch.cuda.synchronize()
+    launches_per_step = our_launches_per_step(step, a_d, b_d)
 
     # ---- timed region: device-resident inputs
     gemm_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
@@ -285,6 +357,7 @@ def main() -> int:
         value = world * macs * args.steps / (ms_max / 1e3)
         e2e_v = world * macs * args.steps / (e2e_max / 1e3)
         pk, pk_kind = peaks()
+        # stage 1 is M*N*K fp16 tensor-core MACs (2 flops each); emul_fn's launches are timed together
         achieved = 2.0 * macs / (gemm_max / 1e3) / 1e12
         peak = pk.get("bf16_tflops", 1590.0)
         cpu = None
@@ -295,20 +368,23 @@ def main() -> int:
             except Exception as e:  # reported, not fatal
                 cpu = {"value": None, "error": f"{type(e).__name__}: {e}"}
         line = {
-            "metric": "emulated FP4 GEMM MAC/s at 8192^3",
+            "metric": "emulated FP4 GEMM MAC/s at 8192^3" if (M, N, K) == (8192, 8192, 8192)
+                      else f"emulated FP4 GEMM MAC/s at {M}x{N}x{K} (profiling size)",
             "value": value, "unit": "MAC/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "int32/f64", "data": "synthetic",
-            "config": {"workload": "NVFP4 emulated GEMM M=N=K=8192 per GPU, fp16 A/B |N(0,1)| with 1% outlier "
+            "config": {"workload": f"NVFP4 emulated GEMM M={M} N={N} K={K} per GPU, fp16 A/B |N(0,1)| with 1% outlier "
                                    "columns x100, quant_fn + emul_fn per step, fp16 out",
                        "M": M, "N": N, "K": K, "format": "nvfp4", "w_reduce": 4, "rounding": "RZ/RZ",
                        "l2": "inputs larger than L2 (fp16 A+B = 268 MB read per step)",
                        "parallelism": f"independent case per GPU x{world}"},
             "e2e": {"value": e2e_v, "unit": "MAC/s", "h2d_bytes_per_step": 2 * M * K * 2, "d2h_bytes_per_step": M * N * 2},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                         "frac": achieved / peak, "traffic": None, "kernel": "emul_gemm",
-                         "kernel_ms": gemm_max, "peak_kind": f"bf16 dense burst ({pk_kind})"},
-            "gpu_launches": 6 * args.steps,
+                         "frac": achieved / peak, "traffic": ncu_traffic() if (M, N, K) == (8192, 8192, 8192) else None,
+                         "kernel": "emul_fn launches (pre-pass kernels + emul_gemm_tc_kernel), CUDA events",
+                         "kernel_ms": gemm_max, "work_per_launch": "2*M*N*K stage-1 tensor-core flops",
+                         "peak_kind": f"bf16 dense burst, {pk_kind}"},
+            "gpu_launches": None if launches_per_step is None else launches_per_step * args.steps,
             "clocks": clk.summary(),
         }
         if cpu is not None:
