@@ -25,7 +25,8 @@ EMU_DTYPE_F16, EMU_DTYPE_BF16 = 0, 1
 ABI_VERSION = 1
 
 SYMBOLS = ("emu_abi_version", "emu_last_error", "emu_status_string", "emu_gemm", "emu_gemm_workspace_size",
-           "emu_gemm_ws", "emu_nvfp4_global_scales", "emu_quant_nvfp4", "emu_quant_mxfp4")
+           "emu_gemm_ws", "emu_gemm_static", "emu_nvfp4_global_scales", "emu_quant_nvfp4", "emu_quant_mxfp4")
+STATIC_SCRATCH_BYTES = 64 << 20   # EMU_STATIC_SCRATCH_BYTES
 
 
 class EmuGemmParams(ctypes.Structure):
@@ -72,6 +73,9 @@ def load() -> ctypes.CDLL:
         L.emu_gemm_ws.restype = i32
         L.emu_gemm_ws.argtypes = [vp, vp, vp, vp, i64, i64, i64, i64, i64, i64, i64, vp,
                                   ctypes.POINTER(EmuGemmParams), vp, vp, ctypes.c_size_t, vp]
+        L.emu_gemm_static.restype = i32
+        L.emu_gemm_static.argtypes = [vp, vp, vp, vp, i64, i64, i64, i64, i64, i64, i64, vp,
+                                      ctypes.POINTER(EmuGemmParams), vp, vp]
         L.emu_nvfp4_global_scales.restype = i32
         L.emu_nvfp4_global_scales.argtypes = [vp, i64, vp, i64, i32, vp, vp, vp, vp]
         L.emu_quant_nvfp4.restype = i32

@@ -38,6 +38,11 @@ bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p
 
 }  // namespace
 
+emu_status emu::record_failure(emu_status s, const char* message) {
+  g_last_error = message;
+  return s;
+}
+
 extern "C" {
 
 int32_t emu_abi_version(void) { return EMU_ABI_VERSION; }

@@ -29,6 +29,9 @@ cudaError_t launch_gemm_tc(const uint8_t* A, const uint8_t* B, const uint8_t* SA
 cudaError_t launch_quant(int sf_vec, const void* x, int dtype, int64_t M, int64_t K,
                          const float* global_scale, uint8_t* q, uint8_t* sf, cudaStream_t stream);
 
+// sets emu_last_error() of the calling thread to `message` and returns s (capi.cu)
+int32_t record_failure(int32_t s, const char* message);
+
 cudaError_t launch_global_scales(const void* a, int64_t a_numel, const void* b, int64_t b_numel,
                                  int dtype, float* gs_a, float* gs_b, float* alpha,
                                  cudaStream_t stream);

@@ -122,6 +122,32 @@ EMU_API emu_status emu_gemm_ws(const uint8_t* a_fp4, const uint8_t* b_fp4, const
                        void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * Bytes of the per-device static scratch behind emu_gemm_static (64 MiB).
+ */
+#define EMU_STATIC_SCRATCH_BYTES (64u << 20)
+
+/*
+ * emu_gemm that allocates nothing: the tensor-core path with its scratch in a static device array
+ * of EMU_STATIC_SCRATCH_BYTES inside the library, for callers that cannot allocate device memory
+ * (FFI hosts without a caching allocator, where cudaMalloc/cudaFree would synchronise the device;
+ * processes whose memory pools already hold the device).  Problems taking the CUDA-core path run
+ * it (it needs no scratch).  No reference counterpart: the reference allocates its outputs and
+ * temporaries through torch.
+ *   - Problems whose emu_gemm_workspace_size exceeds EMU_STATIC_SCRATCH_BYTES fail with
+ *     EMU_ERR_UNSUPPORTED (use emu_gemm_ws).
+ *   - The first call on each device, with that device current, resolves the scratch address
+ *     (cudaGetSymbolAddress, which may load the library's module); make it before any stream capture.
+ *   - One scratch per device: calls whose executions overlap on a device (different streams or
+ *     threads) race on it and must be serialised by the caller.
+ *   - Nothing needs to be zeroed beforehand: each call clears its own flag words on `stream`.
+ * Same arguments, validation and results (bit for bit) as emu_gemm.
+ */
+EMU_API emu_status emu_gemm_static(const uint8_t* a_fp4, const uint8_t* b_fp4, const uint8_t* scale_a,
+                           const uint8_t* scale_b, int64_t M, int64_t N, int64_t K, int64_t scale_a_rows,
+                           int64_t scale_a_cols, int64_t scale_b_rows, int64_t scale_b_cols,
+                           const float* alpha, const emu_gemm_params* params, void* out, void* stream);
+
+/*
  * NVFP4 global scale and GEMM alpha, on the device, without host synchronisation.
  * Replaces gemm_compare/backends/nvfp.py:24-27 global_scale_nvfp and nvfp.py:174-177:
  *   gs = f32(2688.0 / amax) in double, amax = max|x| (1.0 when amax is 0 or NaN),
