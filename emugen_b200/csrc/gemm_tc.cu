@@ -68,8 +68,10 @@ constexpr int GROUP_M = 16;                             // tile raster: 16 M-til
 constexpr int CR_SBQ = 0, CR_KC = 1024, CR_CS = 1280, CR_SBW = 1792, CR_BYTES = 3840;
 // Row record of one (K block, 128-row tile):
 //   double2 rs[128]      row base {exponent word of 2^(52+e) (high half), (2^52 + 2^31) * 2^e}
-//   float   mq[GPB][128] ma * 2^(ea_g - ea)                        (integer path)
-constexpr int RR_RS = 0, RR_MQ = 2048, RR_BYTES = 4096;
+constexpr int RR_RS = 0, RR_BYTES = 2048;
+// Per-block path code (decide kernel): bits 0-1 the epilogue path, bit 2 set when the accumulator
+// provably stays in the f32 normal range (always for NVFP4), so 24-bit rounding in f64 is exact.
+constexpr uint8_t PATH_F64 = 0, PATH_INT = 1, PATH_SUM = 2, PATH_NORMAL = 4;
 // Constant bias tiles for the block-sum path: A row r = {3072, 0, ...}, B row n = {4096, 0, ...} in
 // the 128-byte-swizzled K-major layout, so one K=16 MMA writes 3072 * 4096 = 1.5 * 2^23 everywhere.
 constexpr int BIAS_BYTES = A_BYTES + B_BYTES;
@@ -145,7 +147,9 @@ struct PrepTables {
   uint32_t* cts;        // [tiles_n][G]
   float2* ctm;          // [tiles_n][G]
   uint8_t* ctinf;       // [tiles_n][nb]
-  uint8_t* path;        // [tiles_m][tiles_n][nb]  1 = integer path
+  uint8_t* path;        // [tiles_m][tiles_n][nb]  path code
+  uint32_t* rng_r;      // [tiles_m][2]  MXFP4: max scale byte, 255 - min scale byte (zeroed per call)
+  uint32_t* rng_c;      // [tiles_n][2]
 };
 
 // E4M3 -> (signed significand, exponent) with value = ma * 2^sx; NaN -> ma 0.
@@ -171,6 +175,20 @@ __device__ __forceinline__ double2 row_base(int e) {
   return r;
 }
 
+// MXFP4: fold this thread's scale bytes into its tile's {max byte, 255 - min byte}.  The lanes of a
+// warp always belong to one tile (tiles are multiples of 32 rows / columns).
+__device__ __forceinline__ void scale_range(const uint32_t* byte, int n, uint32_t* rng) {
+  uint32_t mx = 0, mn = 255;
+  for (int g = 0; g < n; ++g) { mx = max(mx, byte[g]); mn = min(mn, byte[g]); }
+  const unsigned mask = __activemask();
+  mx = __reduce_max_sync(mask, mx);
+  mn = __reduce_min_sync(mask, mn);
+  if ((threadIdx.x & 31) == __ffs(mask) - 1) {
+    atomicMax(&rng[0], mx);
+    atomicMax(&rng[1], 255u - mn);
+  }
+}
+
 // one thread per (row, block)
 template <int FMT>
 __global__ void row_tables_kernel(const uint8_t* __restrict__ sf, int64_t M, int64_t Mp, int64_t G, int64_t nb,
@@ -181,11 +199,8 @@ __global__ void row_tables_kernel(const uint8_t* __restrict__ sf, int64_t M, int
     const int64_t kb = i / Mp, r = i % Mp;
     uint8_t* rec = t.rowrec + (kb * tiles_m + r / BM) * RR_BYTES;
     double2* rs = reinterpret_cast<double2*>(rec + RR_RS) + r % BM;
-    float* mq = reinterpret_cast<float*>(rec + RR_MQ) + r % BM;
     if (r >= M) {   // rows of the last tile beyond M: finite, discarded by the epilogue
       *rs = row_base(0);
-#pragma unroll
-      for (int g = 0; g < GPB; ++g) mq[g * BM] = 0.0f;
       continue;
     }
     uint32_t byte[GPB];
@@ -204,9 +219,7 @@ __global__ void row_tables_kernel(const uint8_t* __restrict__ sf, int64_t M, int
       if (base == (1 << 30)) base = 0;
 #pragma unroll
       for (int g = 0; g < GPB; ++g) {
-        const float q = ma[g] == 0 ? 0.0f : (float)ma[g] * (float)(1 << (sx[g] - base));
-        t.rmaq[r * G + kb * GPB + g] = q;
-        mq[g * BM] = q;
+        t.rmaq[r * G + kb * GPB + g] = ma[g] == 0 ? 0.0f : (float)ma[g] * (float)(1 << (sx[g] - base));
         RowScaleNv rec;
         rec.ma = (float)ma[g];
         rec.hi = (uint32_t)(sx[g] + 1073) << 20;
@@ -227,13 +240,13 @@ __global__ void row_tables_kernel(const uint8_t* __restrict__ sf, int64_t M, int
 #pragma unroll
       for (int g = 0; g < GPB; ++g) {
         const int d = (int)byte[g] - base;
-        const float q = (byte[g] == 255u) ? 0.0f : __int_as_float((min(d, 126) + 127) << 23);   // 2^126 sentinel:
-        t.rmaq[r * G + kb * GPB + g] = q;                            // finite, fails the bounds unless the data is 0
-        mq[g * BM] = q;
+        // 2^126 sentinel: finite, and fails the bounds unless the data is 0
+        t.rmaq[r * G + kb * GPB + g] = (byte[g] == 255u) ? 0.0f : __int_as_float((min(d, 126) + 127) << 23);
         static_cast<double*>(t.rw)[r * G + kb * GPB + g] = ue8m0_quarter_f64(byte[g]);
       }
       *rs = row_base(base - 128);  // v = p4 * 2^(ua+ub-256)
       t.rinf[r * nb + kb] = inf ? 1 : 0;
+      scale_range(byte, GPB, t.rng_r + 2 * (r / BM));
     }
   }
 }
@@ -305,6 +318,7 @@ __global__ void col_tables_kernel(const uint8_t* __restrict__ sf, int64_t N, int
       }
       cs[c] = pow2d(base - 128);
       t.cinf[n * nb + kb] = inf ? 1 : 0;
+      scale_range(byte, GPB, t.rng_c + 2 * tn);
     }
     kc[c] = 0x80000000u - MAGIC_BITS * sum;
   }
@@ -401,11 +415,13 @@ template <int FMT>
 __global__ void decide_kernel(int64_t tiles_m, int64_t tiles_n, int64_t nb, int64_t G, PrepTables t) {
   constexpr int GPB = Fmt<FMT>::GPB;
   const double margin = 1.0 + 0x1p-20;   // covers the f32 rounding of the stored maxima
+  int lg_nb = 0;
+  while ((1ll << lg_nb) < nb) ++lg_nb;
   const int64_t total = tiles_m * tiles_n * nb;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t kb = i % nb, tn = (i / nb) % tiles_n, tm = i / (nb * tiles_n);
     bool ok = !t.rtinf[tm * nb + kb] && !t.ctinf[tn * nb + kb];
-    bool fold = true;
+    bool fold_a = true, fold_b = true;
     double s1 = 0.0, s2 = 0.0;
 #pragma unroll
     for (int g = 0; g < GPB; ++g) {
@@ -416,17 +432,29 @@ __global__ void decide_kernel(int64_t tiles_m, int64_t tiles_n, int64_t nb, int6
       const double p = fmin(l1a * lib, lia * l1b);
       const double tmax = fmin((double)am.x * lib, (double)am.y * l1b) * margin;
       ok = ok && (p < 2048.0) && (tmax < 4194304.0);
-      // block-sum path: folded operands max|2a*ma'| = max Linf*|ma'| must be an exact fp16
-      fold = fold && ((double)am.y * margin <= 65504.0) && ((double)bm.y * margin <= 65504.0);
+      // folded operands: max |2a * ma'| = max Linf * |ma'| (and the B side) must be exact fp16 values
+      fold_a = fold_a && ((double)am.y * margin <= 65504.0);
+      fold_b = fold_b && ((double)bm.y * margin <= 65504.0);
       s1 += (double)am.x * (double)bm.y * margin;
       s2 += (double)am.y * (double)bm.x * margin;
     }
     const double tb = fmin(s1, s2);
-    ok = ok && (tb < 2147483648.0);
-    // the tensor core accumulates 1.5*2^23 + T in f32: exact while every partial sum stays in
-    // (2^23, 2^24), i.e. |partial sums of T| < 2^22, which tb bounds
-    fold = ok && fold && (tb < 4194304.0);
-    t.path[i] = fold ? 2 : (ok ? 1 : 0);
+    ok = ok && fold_a && (tb < 2147483648.0);
+    // the block sum accumulates 1.5*2^23 + T in f32 on the tensor core: exact while every partial sum
+    // stays in (2^23, 2^24), i.e. |partial sums of T| < 2^22, which tb bounds
+    const bool sum = ok && fold_b && (tb < 4194304.0);
+    uint8_t code = sum ? PATH_SUM : (ok ? PATH_INT : PATH_F64);
+    if (FMT == EMU_FMT_NVFP4) {
+      code |= PATH_NORMAL;   // |acc| < 2^40 and every term a multiple of 2^-20: always in range
+    } else {
+      // every block term is a multiple of 2^(minA + minB - 256) and at most 9216 * 2^(maxA + maxB - 256):
+      // no accumulator value is subnormal or reaches 2^127 when these hold for the whole tile pair
+      const uint32_t maxa = t.rng_r[2 * tm], mina = 255u - t.rng_r[2 * tm + 1];
+      const uint32_t maxb = t.rng_c[2 * tn], minb = 255u - t.rng_c[2 * tn + 1];
+      if (maxa < 255u && maxb < 255u && mina + minb >= 130u && (int)(maxa + maxb) + 14 + lg_nb <= 382)
+        code |= PATH_NORMAL;
+    }
+    t.path[i] = code;
   }
 }
 
@@ -480,6 +508,29 @@ __device__ __forceinline__ double round_to_f32_in_f64(double x) {
   return (double)round_f64_to_f32(x, RM);
 }
 
+template <int RM, bool FAST>
+__device__ __forceinline__ double round_acc(double x) {
+  return FAST ? round24<RM>(x) : round_to_f32_in_f64<RM>(x);
+}
+
+// Block-sum update of 16 accumulators acc[OFF .. OFF+15] from TMEM words 0x4B400000 + T:
+// T + 2^31 as the low word under the row's exponent word, minus the row constant, is T * 2^e_row
+// exactly; one FMA with the column factor 2^e_col adds it to the accumulator with one rounding.
+template <int RM, bool FAST, int OFF, int CPT>
+__device__ __forceinline__ void sum_update16(double (&acc)[CPT], const float (&v)[16], const double* cs,
+                                             uint32_t rs_hi, double rs_c) {
+#pragma unroll
+  for (int j = 0; j < 16; j += 2) {
+    const double2 c = *reinterpret_cast<const double2*>(&cs[OFF + j]);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const uint32_t lo = __float_as_uint(v[j + h]) + F_TO_T31;
+      const double tf = __dadd_rn(__hiloint2double((int)rs_hi, (int)lo), -rs_c);
+      acc[OFF + j + h] = round_acc<RM, FAST>(__fma_rn(tf, h ? c.y : c.x, acc[OFF + j + h]));
+    }
+  }
+}
+
 // 12 warps: warpgroup 0 = producer (warp 0), MMA issuer and TMEM owner (warp 1), two idle warps;
 // warpgroups 1-2 = 8 epilogue warps, each thread owning one row and 32 columns of the 64-column tile.
 // Registers are moved from warpgroup 0 to the epilogue (setmaxnreg): 128 x 56 + 256 x 224 = the
@@ -497,7 +548,6 @@ emul_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
   constexpr int SET_COLS = GPB * BN;                         // TMEM columns per K block
   constexpr int NSETS = 512 / SET_COLS;                      // 2 (NVFP4) or 4 (MXFP4)
   constexpr uint32_t CR_TX = (FMT == EMU_FMT_NVFP4) ? CR_BYTES : (uint32_t)(CR_SBW + 2 * BN * 8);
-  constexpr uint32_t RR_TX = (uint32_t)(RR_MQ + GPB * BM * 4);
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -564,16 +614,18 @@ emul_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
             ok = ptx::mbar_wait(&empty[s], (uint32_t)((it / NSTAGE) & 1) ^ 1u, p.err, 1);
             if (!ok) break;
             uint8_t* sa = stage_base + s * STAGE_BYTES;
-            const bool fold = p.path[(tm * p.tiles_n + tn) * p.nb + kb] == 2;
+            // block-sum blocks read both folded operands, integer blocks the folded A, f64 blocks neither
+            const int path = p.path[(tm * p.tiles_n + tn) * p.nb + kb] & 3;
             ptx::mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
-            ptx::tma_load_2d(sa, fold ? &tmAF : &tmA, &full[s], (int)(kb * BK), (int)(tm * BM));
-            ptx::tma_load_2d(sa + A_BYTES, fold ? &tmBF : &tmB, &full[s], (int)(kb * BK), (int)(tn * BN));
+            ptx::tma_load_2d(sa, path != PATH_F64 ? &tmAF : &tmA, &full[s], (int)(kb * BK), (int)(tm * BM));
+            ptx::tma_load_2d(sa + A_BYTES, path == PATH_SUM ? &tmBF : &tmB, &full[s], (int)(kb * BK),
+                             (int)(tn * BN));
             const int q = (int)(it % NCR);
             ok = ptx::mbar_wait(&cr_empty[q], (uint32_t)((it / NCR) & 1) ^ 1u, p.err, 2);
             if (!ok) break;
-            ptx::mbar_arrive_expect_tx(&cr_full[q], CR_TX + RR_TX);
+            ptx::mbar_arrive_expect_tx(&cr_full[q], CR_TX + RR_BYTES);
             ptx::bulk_load(cr_ring + q * CR_BYTES, p.colrec + (kb * p.tiles_n + tn) * CR_BYTES, CR_TX, &cr_full[q]);
-            ptx::bulk_load(rr_ring + q * RR_BYTES, p.rowrec + (kb * p.tiles_m + tm) * RR_BYTES, RR_TX, &cr_full[q]);
+            ptx::bulk_load(rr_ring + q * RR_BYTES, p.rowrec + (kb * p.tiles_m + tm) * RR_BYTES, RR_BYTES, &cr_full[q]);
           }
         }
         // drain: every issued copy must have landed before the CTA may exit (bounded waits)
@@ -595,7 +647,7 @@ emul_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
           for (int64_t kb = 0; kb < p.nb && ok; ++kb, ++it) {
             const int s = (int)(it % NSTAGE);
             const int set = (int)(it % NSETS);
-            const bool fold = path_row[kb] == 2;
+            const int path = path_row[kb] & 3;
             ok = ptx::mbar_wait(&tm_empty[set], (uint32_t)((it / NSETS) & 1) ^ 1u, p.err, 3);
             if (!ok) break;
             ok = ptx::mbar_wait(&full[s], (uint32_t)((it / NSTAGE) & 1), p.err, 4);
@@ -604,24 +656,28 @@ emul_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
             const uint32_t a_addr = ptx::smem_u32(stage_base + s * STAGE_BYTES);
             const uint32_t b_addr = a_addr + A_BYTES;
             const uint32_t d_col = tmem_base + (uint32_t)(set * SET_COLS);
-            if (fold) {
+            const uint64_t bias_a = ptx::smem_desc_sw128(ptx::smem_u32(bias_tile));
+            const uint64_t bias_b = ptx::smem_desc_sw128(ptx::smem_u32(bias_tile) + A_BYTES);
+            if (path == PATH_SUM) {
               // block sum: bias 1.5*2^23, then every group accumulated into one accumulator
-              const uint32_t ba = ptx::smem_u32(bias_tile);
-              ptx::mma_f16(d_col, ptx::smem_desc_sw128(ba), ptx::smem_desc_sw128(ba + A_BYTES), IDESC, 0);
-  #pragma unroll
+              ptx::mma_f16(d_col, bias_a, bias_b, IDESC, 0);
+#pragma unroll
               for (int kk = 0; kk < BK / 16; ++kk)
                 ptx::mma_f16(d_col, ptx::smem_desc_sw128(a_addr + 32 * kk), ptx::smem_desc_sw128(b_addr + 32 * kk), IDESC, 1);
-            } else
-  #pragma unroll
-            for (int g = 0; g < GPB; ++g) {
-              const uint32_t d = d_col + (uint32_t)(g * BN);
-              if (FMT == EMU_FMT_NVFP4) {
-                // group g: K elements [16g, 16g+16) = bytes [32g, 32g+32) of each 128-byte row
-                ptx::mma_f16(d, ptx::smem_desc_sw128(a_addr + 32 * g), ptx::smem_desc_sw128(b_addr + 32 * g), IDESC, 0);
-              } else {
-                ptx::mma_f16(d, ptx::smem_desc_sw128(a_addr + 64 * g), ptx::smem_desc_sw128(b_addr + 64 * g), IDESC, 0);
-                ptx::mma_f16(d, ptx::smem_desc_sw128(a_addr + 64 * g + 32), ptx::smem_desc_sw128(b_addr + 64 * g + 32),
-                             IDESC, 1);
+            } else {
+              // one accumulator per group; integer blocks start each from the 1.5*2^23 bias
+              constexpr int KPG = Fmt<FMT>::GS / 16;   // K16 steps per group
+#pragma unroll
+              for (int g = 0; g < GPB; ++g) {
+                const uint32_t d = d_col + (uint32_t)(g * BN);
+                if (path == PATH_INT) ptx::mma_f16(d, bias_a, bias_b, IDESC, 0);
+#pragma unroll
+                for (int kk = 0; kk < KPG; ++kk) {
+                  // K elements [GS*g + 16*kk, +16) = bytes [2*GS*g + 32*kk, +32) of each 128-byte row
+                  const uint32_t off = (uint32_t)(2 * Fmt<FMT>::GS * g + 32 * kk);
+                  ptx::mma_f16(d, ptx::smem_desc_sw128(a_addr + off), ptx::smem_desc_sw128(b_addr + off), IDESC,
+                               (path == PATH_INT || kk > 0) ? 1u : 0u);
+                }
               }
             }
             ptx::mma_commit(&empty[s]);
@@ -659,7 +715,10 @@ emul_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
         const int set = (int)(it % NSETS);
         const int q = (int)(it % NCR);
         const int pcode = nx_path;
-        const bool ipath = pcode != 0;
+        const int path = pcode & 3;
+        const bool ipath = path == PATH_INT;
+        // 24-bit rounding in f64 is exact when the accumulator provably stays in the f32 normal range
+        const bool fast = (FMT == EMU_FMT_NVFP4) || (pcode & PATH_NORMAL);
         if (kb + 1 < p.nb) nx_path = path_row[kb + 1];
         ok = __all_sync(0xFFFFFFFFu, ptx::mbar_wait(&tm_full[set], (uint32_t)((it / NSETS) & 1), p.err, 5));
         if (!ok) break;
@@ -676,33 +735,47 @@ emul_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
         const uint32_t rs_hi = (uint32_t)__double2hiint(rsv.x);
         const double rs_c = rsv.y;
 
-        if (pcode == 2) {
-          // block-sum path: one TMEM word per output, = 0x4B400000 + T
+        if (path == PATH_SUM) {
+          // block-sum path: one TMEM word per output, all 32 loaded before a single wait
+          static_assert(CPT == 32, "two 16-column halves");
+          if (FMT == EMU_FMT_NVFP4) {
+            // NVFP4 keeps more integer-path state live: 8-column chunks, one wait each
 #pragma unroll
-          for (int c8 = 0; c8 < CPT / 8; ++c8) {
-            float v[8];
-            ptx::tmem_ld8(tmem_base + lane_base + (uint32_t)(set * SET_COLS + col0 + c8 * 8), v);
-            ptx::tmem_wait_ld();
-            if (c8 == CPT / 8 - 1) {
-              ptx::tc_fence_before();
-              __syncwarp();
-              if (lane == 0) ptx::mbar_arrive(&tm_empty[set]);
-            }
+            for (int c8 = 0; c8 < CPT / 8; ++c8) {
+              float v[8];
+              ptx::tmem_ld8(tmem_base + lane_base + (uint32_t)(set * SET_COLS + col0 + c8 * 8), v);
+              ptx::tmem_wait_ld();
+              if (c8 == CPT / 8 - 1) {
+                ptx::tc_fence_before();
+                __syncwarp();
+                if (lane == 0) ptx::mbar_arrive(&tm_empty[set]);
+              }
 #pragma unroll
-            for (int j4 = 0; j4 < 2; ++j4) {
-              const int cb = col0 + c8 * 8 + j4 * 4;
-              const double2 c01 = *reinterpret_cast<const double2*>(&cs[cb]);
-              const double2 c23 = *reinterpret_cast<const double2*>(&cs[cb + 2]);
+              for (int j = 0; j < 8; j += 2) {
+                const double2 c = *reinterpret_cast<const double2*>(&cs[col0 + c8 * 8 + j]);
 #pragma unroll
-              for (int jj = 0; jj < 4; ++jj) {
-                const int j = c8 * 8 + j4 * 4 + jj;
-                const double cv = jj == 0 ? c01.x : jj == 1 ? c01.y : jj == 2 ? c23.x : c23.y;
-                const uint32_t lo = __float_as_uint(v[j4 * 4 + jj]) + F_TO_T31;
-                const double tf = __dadd_rn(__hiloint2double((int)rs_hi, (int)lo), -rs_c);
-                const double x = __fma_rn(tf, cv, acc[j]);
-                acc[j] = (FMT == EMU_FMT_NVFP4) ? round24<RM>(x) : round_to_f32_in_f64<RM>(x);
+                for (int h = 0; h < 2; ++h) {
+                  const uint32_t lo = __float_as_uint(v[j + h]) + F_TO_T31;
+                  const double tf = __dadd_rn(__hiloint2double((int)rs_hi, (int)lo), -rs_c);
+                  acc[c8 * 8 + j + h] = round24<RM>(__fma_rn(tf, h ? c.y : c.x, acc[c8 * 8 + j + h]));
+                }
               }
             }
+          } else {
+          float v0[16], v1[16];
+          ptx::tmem_ld16(tmem_base + lane_base + (uint32_t)(set * SET_COLS + col0), v0);
+          ptx::tmem_ld16(tmem_base + lane_base + (uint32_t)(set * SET_COLS + col0 + 16), v1);
+          ptx::tmem_wait_ld();
+          ptx::tc_fence_before();
+          __syncwarp();
+          if (lane == 0) ptx::mbar_arrive(&tm_empty[set]);
+          if (fast) {
+            sum_update16<RM, true, 0>(acc, v0, cs + col0, rs_hi, rs_c);
+            sum_update16<RM, true, 16>(acc, v1, cs + col0, rs_hi, rs_c);
+          } else {
+            sum_update16<RM, false, 0>(acc, v0, cs + col0, rs_hi, rs_c);
+            sum_update16<RM, false, 16>(acc, v1, cs + col0, rs_hi, rs_c);
+          }
           }
         } else
 #pragma unroll
@@ -718,9 +791,6 @@ emul_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
             if (lane == 0) ptx::mbar_arrive(&tm_empty[set]);
           }
           if (ipath) {
-            float mq[GPB];
-#pragma unroll
-            for (int g = 0; g < GPB; ++g) mq[g] = reinterpret_cast<const float*>(rr + RR_MQ)[g * BM + rl];
 #pragma unroll
             for (int j4 = 0; j4 < 2; ++j4) {
               const int cb = col0 + c8 * 8 + j4 * 4;
@@ -733,18 +803,17 @@ emul_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
 #pragma unroll
               for (int jj = 0; jj < 4; ++jj) {
                 const int j = c8 * 8 + j4 * 4 + jj;
-                int s32 = 0;
+                const uint32_t kv = jj == 0 ? k4.x : jj == 1 ? k4.y : jj == 2 ? k4.z : k4.w;
+                uint32_t s32 = kv;
 #pragma unroll
                 for (int g = 0; g < GPB; ++g) {
                   const int qv = jj == 0 ? sq[g].x : jj == 1 ? sq[g].y : jj == 2 ? sq[g].z : sq[g].w;
-                  const float bits = __fmaf_rn(v[g][j4 * 4 + jj], mq[g], MAGIC_F);
-                  s32 += __float_as_int(bits) * qv;
+                  s32 += __float_as_uint(v[g][j4 * 4 + jj]) * (uint32_t)qv;
                 }
-                const uint32_t kv = jj == 0 ? k4.x : jj == 1 ? k4.y : jj == 2 ? k4.z : k4.w;
                 const double cv = jj == 0 ? c01.x : jj == 1 ? c01.y : jj == 2 ? c23.x : c23.y;
-                const double tf = __dadd_rn(__hiloint2double((int)rs_hi, (int)((uint32_t)s32 + kv)), -rs_c);
+                const double tf = __dadd_rn(__hiloint2double((int)rs_hi, (int)s32), -rs_c);
                 const double x = __fma_rn(tf, cv, acc[j]);
-                acc[j] = (FMT == EMU_FMT_NVFP4) ? round24<RM>(x) : round_to_f32_in_f64<RM>(x);
+                acc[j] = fast ? round24<RM>(x) : round_to_f32_in_f64<RM>(x);
               }
             }
           } else {
@@ -862,7 +931,7 @@ static size_t align_up(size_t x) { return (x + 1023) & ~(size_t)1023; }
 
 struct WsLayout {
   size_t a16, b16, af16, bf16, rmaq, rowrec, rw, row_nan, rinf, colrec, col_nan, cinf, ast, bst, rts, rtm, rtinf, cts, ctm, ctinf,
-      path, err, zero_begin, zero_end, total;
+      path, rng_r, rng_c, err, zero_begin, zero_end, total;
 };
 
 static WsLayout layout(int fmt, int64_t M, int64_t N, int64_t K) {
@@ -894,6 +963,8 @@ static WsLayout layout(int fmt, int64_t M, int64_t N, int64_t K) {
   L.zero_begin = off;                       // regions cleared before every call
   L.row_nan = take((size_t)M * 4);
   L.col_nan = take((size_t)Np * 4);
+  L.rng_r = take((size_t)tiles_m * 8);
+  L.rng_c = take((size_t)tiles_n * 8);
   L.err = take(16);
   L.zero_end = off;
   L.total = off;
@@ -945,6 +1016,8 @@ static cudaError_t run_tc(const uint8_t* A, const uint8_t* B, const uint8_t* SA,
   T.ctm = reinterpret_cast<float2*>(ws + L.ctm);
   T.ctinf = ws + L.ctinf;
   T.path = ws + L.path;
+  T.rng_r = reinterpret_cast<uint32_t*>(ws + L.rng_r);
+  T.rng_c = reinterpret_cast<uint32_t*>(ws + L.rng_c);
 
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
