@@ -21,11 +21,12 @@ EMU_OK = 0
 EMU_FMT_NVFP4, EMU_FMT_MXFP4 = 0, 1
 EMU_RZ, EMU_RNE = 0, 1
 EMU_OUT_F16, EMU_OUT_BF16_VIA_F16, EMU_OUT_F32 = 0, 1, 2
-EMU_DTYPE_F16, EMU_DTYPE_BF16 = 0, 1
+EMU_DTYPE_F16, EMU_DTYPE_BF16, EMU_DTYPE_F32 = 0, 1, 2
 ABI_VERSION = 1
 
 SYMBOLS = ("emu_abi_version", "emu_last_error", "emu_status_string", "emu_gemm", "emu_gemm_workspace_size",
-           "emu_gemm_ws", "emu_gemm_static", "emu_nvfp4_global_scales", "emu_quant_nvfp4", "emu_quant_mxfp4")
+           "emu_gemm_ws", "emu_gemm_static", "emu_nvfp4_global_scales", "emu_quant_nvfp4", "emu_quant_mxfp4",
+           "emu_compare", "emu_dequant_fp4")
 STATIC_SCRATCH_BYTES = 64 << 20   # EMU_STATIC_SCRATCH_BYTES
 
 
@@ -33,6 +34,12 @@ class EmuGemmParams(ctypes.Structure):
     _fields_ = [("format", ctypes.c_int32), ("group_size", ctypes.c_int32), ("w_reduce", ctypes.c_int32),
                 ("stage3_rounding", ctypes.c_int32), ("stage4_rounding", ctypes.c_int32),
                 ("out_mode", ctypes.c_int32)]
+
+
+class EmuCompareStats(ctypes.Structure):
+    _fields_ = [("mismatches", ctypes.c_int64), ("first_index", ctypes.c_int64), ("max_diff", ctypes.c_float),
+                ("max_sq_error", ctypes.c_float), ("sq_error_sum", ctypes.c_double), ("ref_sq_sum", ctypes.c_double),
+                ("numel", ctypes.c_int64)]
 
 
 class EmuError(RuntimeError):
@@ -82,6 +89,10 @@ def load() -> ctypes.CDLL:
         L.emu_quant_nvfp4.argtypes = [vp, i32, i64, i64, vp, vp, vp, vp]
         L.emu_quant_mxfp4.restype = i32
         L.emu_quant_mxfp4.argtypes = [vp, i32, i64, i64, vp, vp, vp]
+        L.emu_compare.restype = i32
+        L.emu_compare.argtypes = [vp, vp, i32, i64, vp, vp]
+        L.emu_dequant_fp4.restype = i32
+        L.emu_dequant_fp4.argtypes = [vp, vp, i64, i64, i64, i32, vp, vp, vp]
         v = L.emu_abi_version()
         if v != ABI_VERSION:
             raise ImportError(f"libemugen ABI version {v}, expected {ABI_VERSION}: rebuild it")
@@ -222,3 +233,50 @@ def quant_nvfp4(x: torch.Tensor, global_scale: torch.Tensor):
 def quant_mxfp4(x: torch.Tensor):
     """x [M, K] fp16/bf16 -> (q uint8 [M, K/2], sf uint8 [pad128(M), pad4(K/32)] swizzled UE8M0)."""
     return _quant(x, 32, None)
+
+
+def _cmp_dtype(t: torch.Tensor) -> int:
+    codes = {torch.float16: EMU_DTYPE_F16, torch.bfloat16: EMU_DTYPE_BF16, torch.float32: EMU_DTYPE_F32}
+    if t.dtype not in codes:
+        raise RuntimeError(f"compare supports float16, bfloat16 and float32 tensors, got {t.dtype}")
+    return codes[t.dtype]
+
+
+def compare_stats(ref: torch.Tensor, out: torch.Tensor) -> dict:
+    """emu_compare on the device: mismatch count, first mismatch index, max |diff|, squared-error sums.
+    Both tensors are moved to one CUDA device (the first CUDA one given) and must share shape and dtype."""
+    L = load()
+    if ref.shape != out.shape:
+        raise RuntimeError(f"shape mismatch: {tuple(ref.shape)} vs {tuple(out.shape)}")
+    if ref.dtype != out.dtype:
+        raise RuntimeError(f"dtype mismatch: {ref.dtype} vs {out.dtype}")
+    dev = _device_for(ref, out)
+    r = ref.to(dev).contiguous()
+    o = out.to(dev).contiguous()
+    st = torch.empty(ctypes.sizeof(EmuCompareStats), dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        status = L.emu_compare(r.data_ptr(), o.data_ptr(), _cmp_dtype(r), r.numel(), st.data_ptr(), _stream(dev))
+    _check(status)
+    host = EmuCompareStats.from_buffer_copy(bytes(st.cpu().numpy()))
+    return {k: getattr(host, k) for k, _ in EmuCompareStats._fields_}
+
+
+def dequant_fp4(q: torch.Tensor, sf: torch.Tensor, *, fmt: int, global_scale: torch.Tensor | None = None
+                ) -> torch.Tensor:
+    """Packed e2m1 [rows, K/2] + swizzled scales -> f32 [rows, K] on the device (emu_dequant_fp4)."""
+    L = load()
+    dev = _device_for(q, sf)
+    q_ = _bytes2d(q, dev, "q")
+    sf_ = _bytes2d(sf, dev, "sf")
+    rows, K = q_.shape[0], q_.shape[1] * 2
+    out = torch.empty((rows, K), dtype=torch.float32, device=dev)
+    g = None
+    if fmt == EMU_FMT_NVFP4:
+        if global_scale is None:
+            raise RuntimeError("NVFP4 dequantisation needs the global scale")
+        g = global_scale.reshape(1).to(device=dev, dtype=torch.float32).contiguous()
+    with torch.cuda.device(dev):
+        status = L.emu_dequant_fp4(q_.data_ptr(), sf_.data_ptr(), rows, K, sf_.shape[1], fmt,
+                                   None if g is None else g.data_ptr(), out.data_ptr(), _stream(dev))
+    _check(status)
+    return out

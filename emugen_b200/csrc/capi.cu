@@ -193,4 +193,34 @@ emu_status emu_quant_mxfp4(const void* x, int32_t dtype, int64_t M, int64_t K, u
   return quant_common(32, x, dtype, M, K, nullptr, q, sf, stream);
 }
 
+emu_status emu_compare(const void* ref, const void* out, int32_t dtype, int64_t n, emu_compare_stats* stats,
+                       void* stream) {
+  if (n < 0) return fail(EMU_ERR_INVALID_ARGUMENT, "negative size");
+  if (!stats || (n > 0 && (!ref || !out))) return fail(EMU_ERR_INVALID_ARGUMENT, "pointers must not be NULL");
+  if (dtype != EMU_DTYPE_F16 && dtype != EMU_DTYPE_BF16 && dtype != EMU_DTYPE_F32)
+    return fail(EMU_ERR_INVALID_ARGUMENT, "dtype must be EMU_DTYPE_F16, EMU_DTYPE_BF16 or EMU_DTYPE_F32");
+  if (!aligned(stats, 8)) return fail(EMU_ERR_INVALID_ARGUMENT, "stats must be 8-byte aligned");
+  return cuda_status(emu::launch_compare(ref, out, dtype, n, stats, static_cast<cudaStream_t>(stream)),
+                     "emu_compare launch");
+}
+
+emu_status emu_dequant_fp4(const uint8_t* q, const uint8_t* sf, int64_t rows, int64_t K, int64_t sf_cols,
+                           int32_t format, const float* global_scale, float* out, void* stream) {
+  if (rows < 0 || K < 0 || sf_cols < 0) return fail(EMU_ERR_INVALID_ARGUMENT, "negative size");
+  if (format != EMU_FMT_NVFP4 && format != EMU_FMT_MXFP4)
+    return fail(EMU_ERR_INVALID_ARGUMENT, "unknown format %d", format);
+  const int64_t gsz = format == EMU_FMT_NVFP4 ? 16 : 32;
+  if (K % gsz != 0) return fail(EMU_ERR_K_GROUP, "K must be a multiple of %lld", (long long)gsz);
+  if (rows == 0 || K == 0) return ok();
+  if (!q || !sf || !out || (format == EMU_FMT_NVFP4 && !global_scale))
+    return fail(EMU_ERR_INVALID_ARGUMENT, "pointers must not be NULL");
+  if (sf_cols % 4 != 0 || sf_cols < K / gsz)
+    return fail(EMU_ERR_SCALE_SHAPE, "scale columns (%lld) must be a multiple of 4 and at least K/group (%lld)",
+                (long long)sf_cols, (long long)(K / gsz));
+  if (!aligned(q, 4) || !aligned(out, 16)) return fail(EMU_ERR_INVALID_ARGUMENT, "q must be 4-byte, out 16-byte aligned");
+  return cuda_status(emu::launch_dequant(q, sf, rows, K, sf_cols, format, global_scale, out,
+                                         static_cast<cudaStream_t>(stream)),
+                     "emu_dequant_fp4 launch");
+}
+
 }  // extern "C"

@@ -36,4 +36,9 @@ cudaError_t launch_global_scales(const void* a, int64_t a_numel, const void* b, 
                                  int dtype, float* gs_a, float* gs_b, float* alpha,
                                  cudaStream_t stream);
 
+cudaError_t launch_compare(const void* ref, const void* out, int dtype, int64_t n, emu_compare_stats* stats,
+                           cudaStream_t stream);
+cudaError_t launch_dequant(const uint8_t* q, const uint8_t* sf, int64_t rows, int64_t K, int64_t sf_cols, int fmt,
+                           const float* global_scale, float* out, cudaStream_t stream);
+
 }  // namespace emu

@@ -58,7 +58,8 @@ enum { EMU_RZ = 0, EMU_RNE = 1 };   /* same codes as nvfp_cpp_emul.RZ / RNE */
 enum { EMU_OUT_F16 = 0,             /* fp16, the C++ emulators' output */
        EMU_OUT_BF16_VIA_F16 = 1,    /* bf16(fp16(x)): reference `.to(out_dtype)` after fp16, gemm.py:69 */
        EMU_OUT_F32 = 2 };           /* the f32 accumulator times alpha, before the fp16 rounding */
-enum { EMU_DTYPE_F16 = 0, EMU_DTYPE_BF16 = 1 };  /* quantiser input dtypes */
+enum { EMU_DTYPE_F16 = 0, EMU_DTYPE_BF16 = 1,   /* quantiser input dtypes */
+       EMU_DTYPE_F32 = 2 };                      /* also accepted by emu_compare */
 
 /* Accumulator model of one emulated GEMM (search/emulation/config.py:10-81 and the state fields
  * of gemm_compare/backends/nvfp.py:30-44, mxfp.py:27-42).  w_stage3 / w_stage4 / m_chunk_size are
@@ -177,6 +178,40 @@ EMU_API emu_status emu_quant_nvfp4(const void* x, int32_t dtype, int64_t M, int6
  */
 EMU_API emu_status emu_quant_mxfp4(const void* x, int32_t dtype, int64_t M, int64_t K, uint8_t* q,
                            uint8_t* sf, void* stream);
+
+/*
+ * Element-wise comparison of two [n] tensors (fp16 / bf16 / f32, same dtype), on the device.
+ * Replaces the torch reductions of gemm_compare/runner.py:20-55 compare_tensors and 58-79
+ * compare_mse: an element is a mismatch when it is neither == (so +0 == -0) nor NaN on both sides;
+ * max_diff is max |ref - out| (f32) over the mismatches with NaN differences as +inf (0 if none);
+ * the squared-error terms are (ref - out)^2 and ref^2 in f32 with non-finite terms dropped, summed
+ * in f64 (the reference sums in f32: the sums agree to rounding).  `stats` is DEVICE memory the call
+ * overwrites; read it after the stream reaches this point.
+ */
+typedef struct emu_compare_stats {
+  int64_t mismatches;
+  int64_t first_index;     /* row-major index of the first mismatch, -1 if none */
+  float max_diff;
+  float max_sq_error;
+  double sq_error_sum;
+  double ref_sq_sum;
+  int64_t numel;
+} emu_compare_stats;
+
+EMU_API emu_status emu_compare(const void* ref, const void* out, int32_t dtype, int64_t n,
+                               emu_compare_stats* stats, void* stream);
+
+/*
+ * Dequantise packed FP4 to f32: out[r][k] = e2m1(q[r][k]) * scale(r, k / group), scales in the
+ * swizzled layout ([pad128(rows)][sf_cols]).  MXFP4: scale = f32 with bits (u << 23) (u = 0 -> 0,
+ * u = 255 -> inf), as flashinfer.mxfp4_dequantize, the reference's MXFP4 pseudo_fn operand
+ * (gemm_compare/backends/mxfp.py:155-165).  NVFP4: scale = f32(e4m3) / global_scale (device
+ * float[1]), the reference's NVFP4 pseudo_fn operand (gemm_compare/backends/nvfp.py:133-146, whose
+ * nvfp.pseudo_quant module is absent from the reference tree).  K must be a multiple of the group.
+ */
+EMU_API emu_status emu_dequant_fp4(const uint8_t* q, const uint8_t* sf, int64_t rows, int64_t K,
+                                   int64_t sf_cols, int32_t format, const float* global_scale,
+                                   float* out, void* stream);
 
 #ifdef __cplusplus
 }
