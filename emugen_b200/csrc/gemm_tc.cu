@@ -6,30 +6,33 @@
 // NVFP4 w_reduce 4 and MXFP4 w_reduce 2 (one 64-element K block per stage-3 sum).
 //
 // Pre-pass kernels (per call):
-//   unpack_stats    packed e2m1 -> fp16 "2x" integers (exact), plus per (row, group) the L1 and
-//                   max norms of the 2x values, which bound |p4| = |4 * group dot| from above.
-//   row / col       scale tables for both epilogue paths (below) and per-(row|col, block) exponent
-//                   bases; column tables are laid out per (block, 64-column tile) so one bulk copy
-//                   brings a block's column data into shared memory.
+//   unpack_stats    packed e2m1 -> fp16 "2x" integers (exact), plus per (row, group) the L1, max and
+//                   squared L2 norms of the 2x values, which bound |p4| = |4 * group dot| from above.
+//   row / col       scale tables for the epilogue paths (below) and per-(row|col, block) exponent
+//                   bases; row and column records are laid out per (block, tile) so one bulk copy
+//                   each brings a block's row and column data into shared memory.
 //   tile stats      per (128-row | 64-column tile, group) maxima of the norms and multipliers.
-//   decide          per (row tile, column tile, block): integer path or f64 path (below).
+//   decide          per (row tile, column tile, block): block-sum, integer or f64 path (below).
+//   fold rows/cols  the operands times their group multipliers, for the block-sum / integer paths.
 //
 // Main kernel: persistent, one CTA per SM, 12 warps:
-//   warp 0      producer: TMA A [128 x 64] and B [64 x 64] fp16 tiles (128-byte swizzle) into a
-//               6-stage ring; one bulk copy of the block's column record into a 4-stage ring.
-//   warp 1      TMEM owner + MMA issuer: per group one tcgen05.mma kind::f16 M128 N64 K16 (NVFP4;
-//               MXFP4 groups take two, accumulated) into its own TMEM accumulator, so TMEM holds
-//               p4 for every (row, column, group) of the block.  512 columns = a ring of K-block
-//               sets (NVFP4: 2 sets of 4 x 64; MXFP4: 4 sets of 2 x 64).
+//   warp 0      producer: TMA A [128 x 64] and B [64 x 64] fp16 tiles (128-byte swizzle; the folded
+//               or raw operand per the block's path) into a 6-stage ring; bulk copies of the
+//               block's column and row records into a 4-stage ring.
+//   warp 1      TMEM owner + MMA issuer (tcgen05.mma kind::f16 M128 N64 K16): the block-sum path
+//               into one accumulator, the other paths one accumulator per group.  512 columns = a
+//               ring of K-block sets (NVFP4: 2 sets of 4 x 64; MXFP4: 4 sets of 2 x 64).
 //   warps 4-11  epilogue: a thread owns one output row (its TMEM lane) and 32 columns.
 //
-// Integer path (blocks whose tile bounds prove it exact):  per group partial
-//     bits = FFMA(p4, ma * 2^(ea_g - ea), 1.5*2^23)   integer t = p4 * ma * 2^.. in the f32 mantissa
-//     S32  = IMAD(bits, mb * 2^(eb_g - eb), S32)     int32, wraps; the 2^23 bias is removed per block
-//   per block:  T = S32 + K_col (exact integer), Tf = double{2^52, T} - (2^52 + 2^31),
-//     acc = R4(FMA(Tf, 2^ea_row * 2^eb_col, acc))   with the exponent bases of the row and column.
-//   Exactness needs no fp16 rounding (|p4| < 2048), |t| < 2^22 and |T| < 2^31; the decide kernel
-//   checks these with |p4| <= min(L1a*maxb, maxa*L1b) on tile maxima.
+// Block-sum path (tile bounds prove it exact): operands pre-multiplied by the group multipliers
+//     x' = 2a * ma * 2^(ea_g - ea), y' = 2b * mb * 2^(eb_g - eb) (exact fp16 integers), one bias MMA
+//     writing 1.5*2^23 and the block's four K16 MMAs into ONE accumulator: its f32 word is exactly
+//     0x4B400000 + T, T = sum_g p4_g * ma'_g * mb'_g.  Epilogue per output and block:
+//     Tf = double{2^(52+e_row), T + 2^31} - (2^52 + 2^31) * 2^e_row = T * 2^e_row,
+//     acc = R4(FMA(Tf, 2^e_col, acc)).
+// Integer path: A folded, B raw, one accumulator per group started from the 1.5*2^23 bias, so each
+//     word is 0x4B400000 + p4 * ma'; S32 = sum_g word * mb'_g wraps in int32 and a per-column
+//     constant removes the bias terms: S32 + K_col = T + 2^31.  Then as above.
 // f64 path (any other block):  per group partial
 //     NVFP4: diff = double{2^E(sa), FFMA(p4, ma, 1.5*2^23)} - double{2^E(sa), 2^23 bias} = p*sa
 //            S = FMA(diff, sb, S)
@@ -52,7 +55,7 @@ namespace emu {
 namespace tc {
 
 constexpr int BM = 128, BN = 64, BK = 64;
-constexpr int NSTAGE = 6, NCR = 4;
+constexpr int NSTAGE = 6, NCR = 8;
 constexpr int A_BYTES = BM * BK * 2, B_BYTES = BN * BK * 2;
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;          // 24 KB
 constexpr float MAGIC_F = 12582912.0f;                  // 1.5 * 2^23
@@ -75,7 +78,11 @@ constexpr uint8_t PATH_F64 = 0, PATH_INT = 1, PATH_SUM = 2, PATH_NORMAL = 4;
 // Constant bias tiles for the block-sum path: A row r = {3072, 0, ...}, B row n = {4096, 0, ...} in
 // the 128-byte-swizzled K-major layout, so one K=16 MMA writes 3072 * 4096 = 1.5 * 2^23 everywhere.
 constexpr int BIAS_BYTES = A_BYTES + B_BYTES;
-constexpr int SMEM_BYTES = 1024 + NSTAGE * STAGE_BYTES + BIAS_BYTES + NCR * (CR_BYTES + RR_BYTES) + 256;
+// mbarriers (full/empty per stage, cr_full/cr_empty per record slot, 4 + 4 TMEM-set barriers, drain)
+// and the TMEM address word, after the rings; the leading 1024 bytes cover aligning the base to 1024
+constexpr int BAR_BYTES = (2 * NSTAGE + 2 * NCR + 9) * 8 + 8;
+constexpr int SMEM_BYTES = 1024 + NSTAGE * STAGE_BYTES + BIAS_BYTES + NCR * (CR_BYTES + RR_BYTES) + BAR_BYTES;
+static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
 constexpr uint32_t F_TO_T31 = 0x80000000u - MAGIC_BITS;   // (T + 0x4B400000) + this = T + 2^31 (mod 2^32)
 
 // NVFP4 f64-path row record, one per (row, group).
@@ -98,7 +105,7 @@ __global__ void unpack_stats_kernel(const uint8_t* __restrict__ packed, int64_t 
   const int64_t G = K / GS;
   const int64_t loop = (n8 + 31) / 32 * 32;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < loop; i += (int64_t)gridDim.x * blockDim.x) {
-    uint32_t l1 = 0, li = 0;
+    uint32_t l1 = 0, li = 0, l2 = 0;
     const bool live = i < n8;
     if (live) {
       const uint2 w = reinterpret_cast<const uint2*>(packed)[i];
@@ -112,6 +119,7 @@ __global__ void unpack_stats_kernel(const uint8_t* __restrict__ packed, int64_t 
           const uint32_t alo = (uint32_t)abs(lo), ahi = (uint32_t)abs(hi);
           l1 += alo + ahi;
           li = max(li, max(alo, ahi));
+          l2 += alo * alo + ahi * ahi;
           o[4 * h + q] =
               (uint32_t)__half_as_ushort(__int2half_rn(lo)) | ((uint32_t)__half_as_ushort(__int2half_rn(hi)) << 16);
         }
@@ -122,10 +130,11 @@ __global__ void unpack_stats_kernel(const uint8_t* __restrict__ packed, int64_t 
     if (GS == 32) {
       l1 += __shfl_xor_sync(0xFFFFFFFFu, l1, 1);
       li = max(li, __shfl_xor_sync(0xFFFFFFFFu, li, 1));
+      l2 += __shfl_xor_sync(0xFFFFFFFFu, l2, 1);
     }
     if (live && (GS == 16 || (i & 1) == 0)) {
       const int64_t r = i / (K / 16), c = i % (K / 16);
-      stats[r * G + c / (GS / 16)] = l1 | (li << 16);
+      stats[r * G + c / (GS / 16)] = l1 | (li << 10) | (l2 << 14);   // <= 384 | <= 12 | <= 4608
     }
   }
 }
@@ -139,13 +148,13 @@ struct PrepTables {
   uint8_t* colrec;      // [nb][tiles_n][CR_BYTES]
   uint32_t* col_nan;    // [Np]
   uint8_t* cinf;        // [Np][nb]
-  uint32_t* ast;        // [M][G]    L1 | Linf << 16
+  uint32_t* ast;        // [M][G]    L1 | Linf << 10 | L2^2 << 14 of the 2x values
   uint32_t* bst;        // [N][G]
-  uint32_t* rts;        // [tiles_m][G]   max L1 | max Linf << 16 over the tile's rows
-  float2* rtm;          // [tiles_m][G]   max (L1 * |mult|), max (Linf * |mult|) over the rows
+  uint2* rts;           // [tiles_m][G]   {max L1 | max Linf << 16, max L2^2} over the tile's rows
+  float4* rtm;          // [tiles_m][G]   max of L1 * |mult|, Linf * |mult|, L2^2 * mult^2 over the rows
   uint8_t* rtinf;       // [tiles_m][nb]
-  uint32_t* cts;        // [tiles_n][G]
-  float2* ctm;          // [tiles_n][G]
+  uint2* cts;           // [tiles_n][G]
+  float4* ctm;          // [tiles_n][G]
   uint8_t* ctinf;       // [tiles_n][nb]
   uint8_t* path;        // [tiles_m][tiles_n][nb]  path code
   uint32_t* rng_r;      // [tiles_m][2]  MXFP4: max scale byte, 255 - min scale byte (zeroed per call)
@@ -378,14 +387,15 @@ __global__ void tile_stats_kernel(int64_t rows, int64_t tile, int64_t ntiles, in
     const int64_t tl = i / G, g = i % G;
     const int64_t kb = g / GPB;
     const int64_t r0 = tl * tile, r1 = min(rows, r0 + tile);
-    uint32_t l1 = 0, li = 0;
-    float m1 = 0.0f, mi = 0.0f;
+    uint32_t l1 = 0, li = 0, l2 = 0;
+    float m1 = 0.0f, mi = 0.0f, m2 = 0.0f;
     bool inf = false;
     for (int64_t r = r0; r < r1; ++r) {
       const uint32_t s = (is_col ? t.bst : t.ast)[r * G + g];
-      const uint32_t sl1 = s & 0xFFFFu, sli = s >> 16;
+      const uint32_t sl1 = s & 0x3FFu, sli = (s >> 10) & 0xFu, sl2 = s >> 14;
       l1 = max(l1, sl1);
       li = max(li, sli);
+      l2 = max(l2, sl2);
       float mult;
       if (is_col) {
         const uint8_t* rec = t.colrec + (kb * ntiles + tl) * CR_BYTES;
@@ -395,22 +405,26 @@ __global__ void tile_stats_kernel(int64_t rows, int64_t tile, int64_t ntiles, in
         mult = fabsf(t.rmaq[r * G + g]);
         if (FMT == EMU_FMT_MXFP4) inf |= t.rinf[r * nb + kb] != 0;
       }
-      m1 = fmaxf(m1, (float)sl1 * mult);    // products are rounded f32 maxima of values < 2^40: the
-      mi = fmaxf(mi, (float)sli * mult);    // decide kernel compares them with a 2^-20 safety margin
+      m1 = fmaxf(m1, (float)sl1 * mult);    // rounded f32 maxima (inf when out of range): the decide
+      mi = fmaxf(mi, (float)sli * mult);    // kernel compares them with a 2^-20 safety margin
+      m2 = fmaxf(m2, (float)sl2 * mult * mult);
     }
-    (is_col ? t.cts : t.rts)[tl * G + g] = l1 | (li << 16);
-    (is_col ? t.ctm : t.rtm)[tl * G + g] = make_float2(m1, mi);
+    (is_col ? t.cts : t.rts)[tl * G + g] = make_uint2(l1 | (li << 16), l2);
+    (is_col ? t.ctm : t.rtm)[tl * G + g] = make_float4(m1, mi, m2, 0.0f);
     if (g % GPB == 0) (is_col ? t.ctinf : t.rtinf)[tl * nb + kb] = inf ? 1 : 0;
   }
 }
 
-// per (row tile, column tile, block): 1 when the integer path is exact for every output of the block.
-// With L1 / Linf the norms of the 2x values of a group, |p4| <= min(L1a*Linfb, Linfa*L1b), so
-//   (a) no stage-1 fp16 rounding:   max |p4| < 2048
-//   (b) FFMA magic exact:           max |p4 * ma'| < 2^22
-//   (c) no int32 overflow:          max |sum_g p4 * ma' * mb'| < 2^31
-// are implied by the same inequalities on tile maxima of L1, Linf, L1*|ma'|, Linf*|ma'| (rows) and
-// the column counterparts.
+// Path code per (row tile, column tile, block).  With x = 2a, y = 2b the 2x values of one group and
+// L1, Linf, L2 their norms, |p4| = |sum x y| <= min(L1(x) Linf(y), Linf(x) L1(y), L2(x) L2(y)) for
+// every (row, column), and the same holds with the multipliers ma', mb' folded in.  Evaluated on
+// tile maxima of the norms and of the norms times the multipliers:
+//   integer path    no stage-1 fp16 rounding (|p4| < 2048); every per-group word 1.5*2^23 + p4*ma'
+//                   exact in f32 (sum |x ma'| |y| < 2^22); the folded A operand exact in fp16
+//                   (max |x ma'| <= 65504); |T| < 2^31 for the int32 sum;
+//   block-sum path  additionally the folded B operand exact in fp16 and sum |x ma'| |y mb'| < 2^22
+//                   over the whole block, so the f32 accumulation of 1.5*2^23 + T is exact;
+//   f64 path        every other block.
 template <int FMT>
 __global__ void decide_kernel(int64_t tiles_m, int64_t tiles_n, int64_t nb, int64_t G, PrepTables t) {
   constexpr int GPB = Fmt<FMT>::GPB;
@@ -422,23 +436,26 @@ __global__ void decide_kernel(int64_t tiles_m, int64_t tiles_n, int64_t nb, int6
     const int64_t kb = i % nb, tn = (i / nb) % tiles_n, tm = i / (nb * tiles_n);
     bool ok = !t.rtinf[tm * nb + kb] && !t.ctinf[tn * nb + kb];
     bool fold_a = true, fold_b = true;
-    double s1 = 0.0, s2 = 0.0;
+    double s1 = 0.0, s2 = 0.0, s3 = 0.0;
 #pragma unroll
     for (int g = 0; g < GPB; ++g) {
       const int64_t gg = kb * GPB + g;
-      const uint32_t ra = t.rts[tm * G + gg], cb = t.cts[tn * G + gg];
-      const double l1a = ra & 0xFFFFu, lia = ra >> 16, l1b = cb & 0xFFFFu, lib = cb >> 16;
-      const float2 am = t.rtm[tm * G + gg], bm = t.ctm[tn * G + gg];
-      const double p = fmin(l1a * lib, lia * l1b);
-      const double tmax = fmin((double)am.x * lib, (double)am.y * l1b) * margin;
-      ok = ok && (p < 2048.0) && (tmax < 4194304.0);
+      const uint2 ra = t.rts[tm * G + gg], cb = t.cts[tn * G + gg];
+      const double l1a = ra.x & 0xFFFFu, lia = ra.x >> 16, l1b = cb.x & 0xFFFFu, lib = cb.x >> 16;
+      const double l2a = ra.y, l2b = cb.y;   // squared L2 norms, exact integers
+      const float4 am = t.rtm[tm * G + gg], bm = t.ctm[tn * G + gg];
+      // |sum_k x_k y_k| <= min(L1(x) Linf(y), Linf(x) L1(y), L2(x) L2(y)) per (row, column)
+      const bool p_small = fmin(l1a * lib, lia * l1b) < 2048.0 || l2a * l2b < 2048.0 * 2048.0;
+      const double tmax = fmin(fmin((double)am.x * lib, (double)am.y * l1b), sqrt((double)am.z * l2b) * margin) * margin;
+      ok = ok && p_small && (tmax < 4194304.0);
       // folded operands: max |2a * ma'| = max Linf * |ma'| (and the B side) must be exact fp16 values
       fold_a = fold_a && ((double)am.y * margin <= 65504.0);
       fold_b = fold_b && ((double)bm.y * margin <= 65504.0);
       s1 += (double)am.x * (double)bm.y * margin;
       s2 += (double)am.y * (double)bm.x * margin;
+      s3 += sqrt((double)am.z * (double)bm.z) * margin * margin;
     }
-    const double tb = fmin(s1, s2);
+    const double tb = fmin(fmin(s1, s2), s3);
     ok = ok && fold_a && (tb < 2147483648.0);
     // the block sum accumulates 1.5*2^23 + T in f32 on the tensor core: exact while every partial sum
     // stays in (2^23, 2^24), i.e. |partial sums of T| < 2^22, which tb bounds
@@ -513,9 +530,9 @@ __device__ __forceinline__ double round_acc(double x) {
   return FAST ? round24<RM>(x) : round_to_f32_in_f64<RM>(x);
 }
 
-// Block-sum update of 16 accumulators acc[OFF .. OFF+15] from TMEM words 0x4B400000 + T:
-// T + 2^31 as the low word under the row's exponent word, minus the row constant, is T * 2^e_row
-// exactly; one FMA with the column factor 2^e_col adds it to the accumulator with one rounding.
+// Block-sum update of 16 accumulators acc[OFF .. OFF+15] from TMEM words 0x4B400000 + T: the word
+// as the low half under the row's exponent word, minus rs_c = (2^52 + 0x4B400000) * 2^e_row, is
+// T * 2^e_row exactly; one FMA with the column factor 2^e_col adds it with one rounding.
 template <int RM, bool FAST, int OFF, int CPT>
 __device__ __forceinline__ void sum_update16(double (&acc)[CPT], const float (&v)[16], const double* cs,
                                              uint32_t rs_hi, double rs_c) {
@@ -524,26 +541,30 @@ __device__ __forceinline__ void sum_update16(double (&acc)[CPT], const float (&v
     const double2 c = *reinterpret_cast<const double2*>(&cs[OFF + j]);
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
-      const uint32_t lo = __float_as_uint(v[j + h]) + F_TO_T31;
-      const double tf = __dadd_rn(__hiloint2double((int)rs_hi, (int)lo), -rs_c);
+      const double tf = __dadd_rn(__hiloint2double((int)rs_hi, (int)__float_as_uint(v[j + h])), -rs_c);
       acc[OFF + j + h] = round_acc<RM, FAST>(__fma_rn(tf, h ? c.y : c.x, acc[OFF + j + h]));
     }
   }
 }
 
-// 12 warps: warpgroup 0 = producer (warp 0), MMA issuer and TMEM owner (warp 1), two idle warps;
-// warpgroups 1-2 = 8 epilogue warps, each thread owning one row and 32 columns of the 64-column tile.
-// Registers are moved from warpgroup 0 to the epilogue (setmaxnreg): 128 x 56 + 256 x 224 = the
-// 384 x 168 the CTA is launched with.
+// Warpgroup 0 = producer (warp 0), MMA issuer and TMEM owner (warp 1), two idle warps; then EPI
+// epilogue warps, each thread owning one row and CPT = 64 / (EPI / 4) columns of the 64-column tile.
+// Registers move from warpgroup 0 to the epilogue (setmaxnreg); the split never exceeds what the CTA
+// is launched with (LAUNCH_REGS per thread, the largest multiple of 8 that fits the register file).
 // RM: the rounding mode in effect (stage-3 mode for a single K block, else the stage-4 mode).
-constexpr int EPI = 8, NUM_WARPS = 4 + EPI, REG_LOW = 56, REG_HIGH = 224;
-static_assert(128 * REG_LOW + 32 * EPI * REG_HIGH <= 32 * NUM_WARPS * 168, "register split exceeds the launch");
+constexpr int EPI = 8, NUM_WARPS = 4 + EPI;
+constexpr int LAUNCH_REGS = (65536 / (32 * NUM_WARPS)) / 8 * 8;
+constexpr int REG_LOW = 56;
+constexpr int REG_HIGH = ((32 * NUM_WARPS * LAUNCH_REGS - 128 * REG_LOW) / (32 * EPI)) / 8 * 8 > 232
+                             ? 232 : ((32 * NUM_WARPS * LAUNCH_REGS - 128 * REG_LOW) / (32 * EPI)) / 8 * 8;
+static_assert(128 * REG_LOW + 32 * EPI * REG_HIGH <= 32 * NUM_WARPS * LAUNCH_REGS, "register split exceeds the launch");
 template <int FMT, int RM>
 __global__ void __launch_bounds__(32 * NUM_WARPS, 1)
 emul_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ CUtensorMap tmAF, const __grid_constant__ CUtensorMap tmBF, const Params p) {
   constexpr int NUM_EPI_WARPS = EPI;
-  constexpr int CPT = BN / (EPI / 4);                         // columns per epilogue thread
+  constexpr int CPT = BN / (EPI / 4);                         // columns per epilogue thread (16 or 32)
+  constexpr int CW = CPT == 32 ? 16 : 8;                      // integer / f64 path: columns per TMEM trip
   constexpr int GPB = Fmt<FMT>::GPB;
   constexpr int SET_COLS = GPB * BN;                         // TMEM columns per K block
   constexpr int NSETS = 512 / SET_COLS;                      // 2 (NVFP4) or 4 (MXFP4)
@@ -623,8 +644,13 @@ emul_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
             const int q = (int)(it % NCR);
             ok = ptx::mbar_wait(&cr_empty[q], (uint32_t)((it / NCR) & 1) ^ 1u, p.err, 2);
             if (!ok) break;
-            ptx::mbar_arrive_expect_tx(&cr_full[q], CR_TX + RR_BYTES);
-            ptx::bulk_load(cr_ring + q * CR_BYTES, p.colrec + (kb * p.tiles_n + tn) * CR_BYTES, CR_TX, &cr_full[q]);
+            // column record bytes each path reads: block-sum the column factors, integer also the
+            // multipliers and bias constants, f64 the f64 scales as well
+            const uint32_t c_off = path == PATH_SUM ? (uint32_t)CR_CS : 0u;
+            const uint32_t c_len = path == PATH_SUM ? (uint32_t)(BN * 8) : path == PATH_INT ? (uint32_t)(CR_CS + BN * 8) : CR_TX;
+            ptx::mbar_arrive_expect_tx(&cr_full[q], c_len + RR_BYTES);
+            ptx::bulk_load(cr_ring + q * CR_BYTES + c_off, p.colrec + (kb * p.tiles_n + tn) * CR_BYTES + c_off, c_len,
+                           &cr_full[q]);
             ptx::bulk_load(rr_ring + q * RR_BYTES, p.rowrec + (kb * p.tiles_m + tm) * RR_BYTES, RR_BYTES, &cr_full[q]);
           }
         }
@@ -736,64 +762,46 @@ emul_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
         const double rs_c = rsv.y;
 
         if (path == PATH_SUM) {
-          // block-sum path: one TMEM word per output, all 32 loaded before a single wait
-          static_assert(CPT == 32, "two 16-column halves");
-          if (FMT == EMU_FMT_NVFP4) {
-            // NVFP4 keeps more integer-path state live: 8-column chunks, one wait each
-#pragma unroll
-            for (int c8 = 0; c8 < CPT / 8; ++c8) {
-              float v[8];
-              ptx::tmem_ld8(tmem_base + lane_base + (uint32_t)(set * SET_COLS + col0 + c8 * 8), v);
-              ptx::tmem_wait_ld();
-              if (c8 == CPT / 8 - 1) {
-                ptx::tc_fence_before();
-                __syncwarp();
-                if (lane == 0) ptx::mbar_arrive(&tm_empty[set]);
-              }
-#pragma unroll
-              for (int j = 0; j < 8; j += 2) {
-                const double2 c = *reinterpret_cast<const double2*>(&cs[col0 + c8 * 8 + j]);
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                  const uint32_t lo = __float_as_uint(v[j + h]) + F_TO_T31;
-                  const double tf = __dadd_rn(__hiloint2double((int)rs_hi, (int)lo), -rs_c);
-                  acc[c8 * 8 + j + h] = round24<RM>(__fma_rn(tf, h ? c.y : c.x, acc[c8 * 8 + j + h]));
-                }
-              }
-            }
-          } else {
+          // the row constant for words 0x4B400000 + T instead of T + 2^31 (exact: multiples of 2^e)
+          const double rs_c_sum = __fma_rn(-(double)F_TO_T31 * 0x1p-52, __hiloint2double((int)rs_hi, 0), rs_c);
+          // block-sum path: one TMEM word per output; all CPT are loaded before a single wait, so the
+          // TMEM set goes back to the MMA warp after one round trip
+          static_assert(CPT == 16 || CPT == 32, "one or two 16-column halves");
           float v0[16], v1[16];
           ptx::tmem_ld16(tmem_base + lane_base + (uint32_t)(set * SET_COLS + col0), v0);
-          ptx::tmem_ld16(tmem_base + lane_base + (uint32_t)(set * SET_COLS + col0 + 16), v1);
+          if constexpr (CPT == 32) ptx::tmem_ld16(tmem_base + lane_base + (uint32_t)(set * SET_COLS + col0 + 16), v1);
           ptx::tmem_wait_ld();
           ptx::tc_fence_before();
           __syncwarp();
           if (lane == 0) ptx::mbar_arrive(&tm_empty[set]);
-          if (fast) {
-            sum_update16<RM, true, 0>(acc, v0, cs + col0, rs_hi, rs_c);
-            sum_update16<RM, true, 16>(acc, v1, cs + col0, rs_hi, rs_c);
+          if (FMT == EMU_FMT_NVFP4 || fast) {
+            sum_update16<RM, true, 0>(acc, v0, cs + col0, rs_hi, rs_c_sum);
+            if constexpr (CPT == 32) sum_update16<RM, true, 16>(acc, v1, cs + col0, rs_hi, rs_c_sum);
           } else {
-            sum_update16<RM, false, 0>(acc, v0, cs + col0, rs_hi, rs_c);
-            sum_update16<RM, false, 16>(acc, v1, cs + col0, rs_hi, rs_c);
-          }
+            sum_update16<RM, false, 0>(acc, v0, cs + col0, rs_hi, rs_c_sum);
+            if constexpr (CPT == 32) sum_update16<RM, false, 16>(acc, v1, cs + col0, rs_hi, rs_c_sum);
           }
         } else
 #pragma unroll
-        for (int c8 = 0; c8 < CPT / 8; ++c8) {
-          float v[GPB][8];
+        for (int c16 = 0; c16 < CPT / CW; ++c16) {
+          // integer and f64 paths: per group CW columns per round trip (two per block)
+          float v[GPB][CW];
 #pragma unroll
-          for (int g = 0; g < GPB; ++g)
-            ptx::tmem_ld8(tmem_base + lane_base + (uint32_t)(set * SET_COLS + g * BN + col0 + c8 * 8), v[g]);
+          for (int g = 0; g < GPB; ++g) {
+            const uint32_t ta = tmem_base + lane_base + (uint32_t)(set * SET_COLS + g * BN + col0 + c16 * CW);
+            if constexpr (CW == 16) ptx::tmem_ld16(ta, v[g]);
+            else ptx::tmem_ld8(ta, v[g]);
+          }
           ptx::tmem_wait_ld();
-          if (c8 == CPT / 8 - 1) {
+          if (c16 == CPT / CW - 1) {
             ptx::tc_fence_before();
             __syncwarp();
             if (lane == 0) ptx::mbar_arrive(&tm_empty[set]);
           }
           if (ipath) {
 #pragma unroll
-            for (int j4 = 0; j4 < 2; ++j4) {
-              const int cb = col0 + c8 * 8 + j4 * 4;
+            for (int j4 = 0; j4 < CW / 4; ++j4) {
+              const int cb = col0 + c16 * CW + j4 * 4;
               int4 sq[GPB];
 #pragma unroll
               for (int g = 0; g < GPB; ++g) sq[g] = *reinterpret_cast<const int4*>(&sbq[g * BN + cb]);
@@ -802,9 +810,8 @@ emul_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
               const double2 c23 = *reinterpret_cast<const double2*>(&cs[cb + 2]);
 #pragma unroll
               for (int jj = 0; jj < 4; ++jj) {
-                const int j = c8 * 8 + j4 * 4 + jj;
-                const uint32_t kv = jj == 0 ? k4.x : jj == 1 ? k4.y : jj == 2 ? k4.z : k4.w;
-                uint32_t s32 = kv;
+                const int j = c16 * CW + j4 * 4 + jj;
+                uint32_t s32 = jj == 0 ? k4.x : jj == 1 ? k4.y : jj == 2 ? k4.z : k4.w;
 #pragma unroll
                 for (int g = 0; g < GPB; ++g) {
                   const int qv = jj == 0 ? sq[g].x : jj == 1 ? sq[g].y : jj == 2 ? sq[g].z : sq[g].w;
@@ -833,16 +840,16 @@ emul_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
 #pragma unroll
             for (int g = 0; g < GPB; ++g)
 #pragma unroll
-              for (int j = 0; j < 8; ++j) mx = fmaxf(mx, fabsf(v[g][j]));
+              for (int j = 0; j < CW; ++j) mx = fmaxf(mx, fabsf(v[g][j]));
             if (__any_sync(0xFFFFFFFFu, mx >= 2048.0f)) {
 #pragma unroll
               for (int g = 0; g < GPB; ++g)
 #pragma unroll
-                for (int j = 0; j < 8; ++j) v[g][j] = round_p4_f(v[g][j]);
+                for (int j = 0; j < CW; ++j) v[g][j] = round_p4_f(v[g][j]);
             }
 #pragma unroll
-            for (int jj = 0; jj < 8; ++jj) {
-              const int col = col0 + c8 * 8 + jj;
+            for (int jj = 0; jj < CW; ++jj) {
+              const int col = col0 + c16 * CW + jj;
               double S = 0.0;
 #pragma unroll
               for (int g = 0; g < GPB; ++g) {
@@ -858,7 +865,7 @@ emul_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                   S = __fma_rn(__dmul_rn(p4, wsa[g]), sb, S);
                 }
               }
-              const int j = c8 * 8 + jj;
+              const int j = c16 * CW + jj;
               if (FMT == EMU_FMT_NVFP4) {
                 acc[j] = round24<RM>(kb == 0 ? S : __dadd_rn(acc[j], S));
               } else {
@@ -953,11 +960,11 @@ static WsLayout layout(int fmt, int64_t M, int64_t N, int64_t K) {
   L.cinf = take((size_t)Np * nb);
   L.ast = take((size_t)M * G * 4);
   L.bst = take((size_t)N * G * 4);
-  L.rts = take((size_t)tiles_m * G * 4);
-  L.rtm = take((size_t)tiles_m * G * 8);
+  L.rts = take((size_t)tiles_m * G * 8);
+  L.rtm = take((size_t)tiles_m * G * 16);
   L.rtinf = take((size_t)tiles_m * nb);
-  L.cts = take((size_t)tiles_n * G * 4);
-  L.ctm = take((size_t)tiles_n * G * 8);
+  L.cts = take((size_t)tiles_n * G * 8);
+  L.ctm = take((size_t)tiles_n * G * 16);
   L.ctinf = take((size_t)tiles_n * nb);
   L.path = take((size_t)tiles_m * tiles_n * nb);
   L.zero_begin = off;                       // regions cleared before every call
@@ -1009,11 +1016,11 @@ static cudaError_t run_tc(const uint8_t* A, const uint8_t* B, const uint8_t* SA,
   T.cinf = ws + L.cinf;
   T.ast = reinterpret_cast<uint32_t*>(ws + L.ast);
   T.bst = reinterpret_cast<uint32_t*>(ws + L.bst);
-  T.rts = reinterpret_cast<uint32_t*>(ws + L.rts);
-  T.rtm = reinterpret_cast<float2*>(ws + L.rtm);
+  T.rts = reinterpret_cast<uint2*>(ws + L.rts);
+  T.rtm = reinterpret_cast<float4*>(ws + L.rtm);
   T.rtinf = ws + L.rtinf;
-  T.cts = reinterpret_cast<uint32_t*>(ws + L.cts);
-  T.ctm = reinterpret_cast<float2*>(ws + L.ctm);
+  T.cts = reinterpret_cast<uint2*>(ws + L.cts);
+  T.ctm = reinterpret_cast<float4*>(ws + L.ctm);
   T.ctinf = ws + L.ctinf;
   T.path = ws + L.path;
   T.rng_r = reinterpret_cast<uint32_t*>(ws + L.rng_r);
