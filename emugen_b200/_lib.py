@@ -26,7 +26,7 @@ ABI_VERSION = 1
 
 SYMBOLS = ("emu_abi_version", "emu_last_error", "emu_status_string", "emu_gemm", "emu_gemm_workspace_size",
            "emu_gemm_ws", "emu_gemm_static", "emu_nvfp4_global_scales", "emu_quant_nvfp4", "emu_quant_mxfp4",
-           "emu_compare", "emu_dequant_fp4")
+           "emu_gemm_compare", "emu_compare", "emu_dequant_fp4")
 STATIC_SCRATCH_BYTES = 64 << 20   # EMU_STATIC_SCRATCH_BYTES
 
 
@@ -89,6 +89,9 @@ def load() -> ctypes.CDLL:
         L.emu_quant_nvfp4.argtypes = [vp, i32, i64, i64, vp, vp, vp, vp]
         L.emu_quant_mxfp4.restype = i32
         L.emu_quant_mxfp4.argtypes = [vp, i32, i64, i64, vp, vp, vp]
+        L.emu_gemm_compare.restype = i32
+        L.emu_gemm_compare.argtypes = [vp, vp, vp, vp, i64, i64, i64, i64, i64, i64, i64, vp,
+                                       ctypes.POINTER(EmuGemmParams), vp, vp, vp, vp, ctypes.c_size_t, vp]
         L.emu_compare.restype = i32
         L.emu_compare.argtypes = [vp, vp, i32, i64, vp, vp]
         L.emu_dequant_fp4.restype = i32
@@ -280,3 +283,42 @@ def dequant_fp4(q: torch.Tensor, sf: torch.Tensor, *, fmt: int, global_scale: to
                                    None if g is None else g.data_ptr(), out.data_ptr(), _stream(dev))
     _check(status)
     return out
+
+
+def gemm_compare(a_fp4: torch.Tensor, b_fp4: torch.Tensor, scale_a: torch.Tensor, scale_b: torch.Tensor,
+                 ref: torch.Tensor, *, fmt: int, group_size: int, w_reduce: int, stage3_rounding: int,
+                 stage4_rounding: int, alpha: torch.Tensor | None, out_mode: int, write_out: bool = False,
+                 path: str = "auto"):
+    """Emulated GEMM compared with `ref` on the device (emu_gemm_compare).  Returns (stats dict,
+    output or None).  With the tensor-core path and write_out=False the output is never written."""
+    L = load()
+    dev = _device_for(a_fp4, b_fp4, scale_a, scale_b)
+    M, N, K = a_fp4.shape[0], b_fp4.shape[0], a_fp4.shape[1] * 2
+    a = _bytes2d(a_fp4, dev, "a_fp4")
+    b = _bytes2d(b_fp4, dev, "b_fp4")
+    sa = _bytes2d(scale_a, dev, "scale_a")
+    sb = _bytes2d(scale_b, dev, "scale_b")
+    odt = {EMU_OUT_F16: torch.float16, EMU_OUT_BF16_VIA_F16: torch.bfloat16, EMU_OUT_F32: torch.float32}[out_mode]
+    r = ref.to(device=dev).contiguous()
+    if r.dtype != odt or tuple(r.shape) != (M, N):
+        raise RuntimeError(f"ref must be {odt} [{M}, {N}], got {r.dtype} {tuple(r.shape)}")
+    al = None if alpha is None else alpha.detach().reshape(1).to(device=dev, dtype=torch.float32).contiguous()
+    params = EmuGemmParams(fmt, group_size, w_reduce, stage3_rounding, stage4_rounding, out_mode)
+    ws_ptr, ws_bytes, ws = None, 0, None
+    if path == "auto":
+        need = L.emu_gemm_workspace_size(M, N, K, ctypes.byref(params))
+        if need:
+            ws = torch.empty(need + 1024, dtype=torch.uint8, device=dev)
+            ws_ptr = (ws.data_ptr() + 1023) // 1024 * 1024
+            ws_bytes = need
+    out = torch.empty((M, N), dtype=odt, device=dev) if (write_out or ws_ptr is None) else None
+    st = torch.empty(ctypes.sizeof(EmuCompareStats), dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        status = L.emu_gemm_compare(a.data_ptr(), b.data_ptr(), sa.data_ptr(), sb.data_ptr(), M, N, K,
+                                    sa.shape[0], sa.shape[1], sb.shape[0], sb.shape[1],
+                                    None if al is None else al.data_ptr(), ctypes.byref(params), r.data_ptr(),
+                                    None if out is None else out.data_ptr(), st.data_ptr(), ws_ptr, ws_bytes,
+                                    _stream(dev))
+    _check(status)
+    host = EmuCompareStats.from_buffer_copy(bytes(st.cpu().numpy()))
+    return {k: getattr(host, k) for k, _ in EmuCompareStats._fields_}, out

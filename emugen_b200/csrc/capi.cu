@@ -204,6 +204,53 @@ emu_status emu_compare(const void* ref, const void* out, int32_t dtype, int64_t 
                      "emu_compare launch");
 }
 
+emu_status emu_gemm_compare(const uint8_t* a_fp4, const uint8_t* b_fp4, const uint8_t* scale_a,
+                            const uint8_t* scale_b, int64_t M, int64_t N, int64_t K, int64_t scale_a_rows,
+                            int64_t scale_a_cols, int64_t scale_b_rows, int64_t scale_b_cols, const float* alpha,
+                            const emu_gemm_params* params, const void* ref, void* out, emu_compare_stats* stats,
+                            void* workspace, size_t workspace_bytes, void* stream) {
+  emu_status st = validate_gemm(M, N, K, scale_a_rows, scale_a_cols, scale_b_rows, scale_b_cols, params);
+  if (st != EMU_OK) return st;
+  if (!stats || !aligned(stats, 8)) return fail(EMU_ERR_INVALID_ARGUMENT, "stats must be a non-NULL, 8-byte aligned pointer");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (M == 0 || N == 0) {
+    cudaError_t e = emu::launch_compare_init(stats, 0, s);
+    if (e == cudaSuccess) e = emu::launch_compare_fini(stats, s);
+    return cuda_status(e, "emu_gemm_compare");
+  }
+  if (!a_fp4 || !b_fp4 || !scale_a || !scale_b || !ref)
+    return fail(EMU_ERR_INVALID_ARGUMENT, "tensor pointers must not be NULL");
+  if (!aligned(a_fp4, 16) || !aligned(b_fp4, 16))
+    return fail(EMU_ERR_INVALID_ARGUMENT, "a_fp4 / b_fp4 must be 16-byte aligned");
+  const emu_gemm_params p = *params;
+  const int cmp_dtype = p.out_mode == EMU_OUT_F32 ? EMU_DTYPE_F32
+                        : p.out_mode == EMU_OUT_BF16_VIA_F16 ? EMU_DTYPE_BF16 : EMU_DTYPE_F16;
+  if (workspace && tc_path(p, M, N, K)) {
+    if (!aligned(workspace, 1024)) return fail(EMU_ERR_INVALID_ARGUMENT, "workspace must be 1024-byte aligned");
+    if (workspace_bytes < emu::gemm_tc_workspace_size(p.format, M, N, K))
+      return fail(EMU_ERR_INVALID_ARGUMENT, "workspace too small: %zu < %zu bytes", workspace_bytes,
+                  emu::gemm_tc_workspace_size(p.format, M, N, K));
+    emu::GemmArgs args{p.format, p.w_reduce, p.stage3_rounding, p.stage4_rounding, p.out_mode};
+    args.cmp_ref = ref;
+    args.cmp_stats = stats;
+    args.write_out = out != nullptr;
+    cudaError_t e = emu::launch_compare_init(stats, M * N, s);
+    if (e == cudaSuccess)
+      e = emu::launch_gemm_tc(a_fp4, b_fp4, scale_a, scale_b, M, N, K, scale_a_cols, scale_b_cols, alpha, args, out,
+                              workspace, s);
+    if (e == cudaSuccess) e = emu::launch_compare_fini(stats, s);
+    return cuda_status(e, "emu_gemm_compare tensor-core launch");
+  }
+  if (!out)
+    return fail(EMU_ERR_INVALID_ARGUMENT,
+                "out must not be NULL on the CUDA-core path (no workspace, or a shape the tensor-core path does not take)");
+  emu::GemmArgs args{p.format, p.w_reduce, p.stage3_rounding, p.stage4_rounding, p.out_mode};
+  cudaError_t e = emu::launch_gemm_simt(a_fp4, b_fp4, scale_a, scale_b, M, N, K, scale_a_cols, scale_b_cols, alpha,
+                                        args, out, s);
+  if (e == cudaSuccess) e = emu::launch_compare(ref, out, cmp_dtype, M * N, stats, s);
+  return cuda_status(e, "emu_gemm_compare launch");
+}
+
 emu_status emu_dequant_fp4(const uint8_t* q, const uint8_t* sf, int64_t rows, int64_t K, int64_t sf_cols,
                            int32_t format, const float* global_scale, float* out, void* stream) {
   if (rows < 0 || K < 0 || sf_cols < 0) return fail(EMU_ERR_INVALID_ARGUMENT, "negative size");

@@ -76,6 +76,22 @@ __device__ __forceinline__ float round_f64_to_f32(double x, int mode) {
   return mode == EMU_RZ ? __double2float_rz(x) : __double2float_rn(x);
 }
 
+// The output element as a float: y after the output dtype's rounding (what store_output stores).
+__device__ __forceinline__ float output_value(float y, int out_mode) {
+  if (out_mode == EMU_OUT_F32) return y;
+  const __half h = __float2half_rn(y);
+  if (out_mode == EMU_OUT_BF16_VIA_F16) return __bfloat162float(__float2bfloat16_rn(__half2float(h)));
+  return __half2float(h);
+}
+
+// An element of a [*] fp16 / bf16 (EMU_OUT_BF16_VIA_F16) / f32 tensor as a float.
+__device__ __forceinline__ float load_output(const void* p, int64_t i, int out_mode) {
+  if (out_mode == EMU_OUT_F32) return static_cast<const float*>(p)[i];
+  const uint16_t b = static_cast<const uint16_t*>(p)[i];
+  if (out_mode == EMU_OUT_BF16_VIA_F16) return __uint_as_float((uint32_t)b << 16);
+  return __half2float(__ushort_as_half(b));
+}
+
 // Final output conversion: y is the f32 result (already multiplied by alpha).
 __device__ __forceinline__ void store_output(void* out, int64_t idx, float y, int out_mode) {
   if (out_mode == EMU_OUT_F32) {

@@ -146,6 +146,16 @@ unsigned grid_for(int64_t n, int threads) {
 
 }  // namespace
 
+cudaError_t launch_compare_init(emu_compare_stats* stats, int64_t n, cudaStream_t stream) {
+  compare_init_kernel<<<1, 1, 0, stream>>>(stats, n);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_compare_fini(emu_compare_stats* stats, cudaStream_t stream) {
+  compare_fini_kernel<<<1, 1, 0, stream>>>(stats);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_compare(const void* ref, const void* out, int dtype, int64_t n, emu_compare_stats* stats,
                            cudaStream_t stream) {
   compare_init_kernel<<<1, 1, 0, stream>>>(stats, n);

@@ -477,6 +477,9 @@ __global__ void decide_kernel(int64_t tiles_m, int64_t tiles_n, int64_t nb, int6
 
 // ------------------------------------------------------------------------------ main kernel
 struct Params {
+  const void* cmp_ref;           // optional reference output to compare with (fused check)
+  emu_compare_stats* cmp_stats;
+  int write_out;
   int64_t M, N, K;
   int64_t G, nb, tiles_m, tiles_n;
   const uint8_t* rowrec;
@@ -558,7 +561,9 @@ constexpr int REG_LOW = 56;
 constexpr int REG_HIGH = ((32 * NUM_WARPS * LAUNCH_REGS - 128 * REG_LOW) / (32 * EPI)) / 8 * 8 > 232
                              ? 232 : ((32 * NUM_WARPS * LAUNCH_REGS - 128 * REG_LOW) / (32 * EPI)) / 8 * 8;
 static_assert(128 * REG_LOW + 32 * EPI * REG_HIGH <= 32 * NUM_WARPS * LAUNCH_REGS, "register split exceeds the launch");
-template <int FMT, int RM>
+// CMP: the comparison with a reference output is compiled in (a separate instantiation, so the plain
+// GEMM's register allocation is not affected by it).
+template <int FMT, int RM, bool CMP>
 __global__ void __launch_bounds__(32 * NUM_WARPS, 1)
 emul_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ CUtensorMap tmAF, const __grid_constant__ CUtensorMap tmBF, const Params p) {
@@ -879,7 +884,11 @@ emul_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
         if (lane == 0) ptx::mbar_arrive(&cr_empty[q]);
       }
       if (!ok) break;
-      // ---- output
+      // ---- output (and the optional fused comparison with a reference output, emu_compare's rules)
+      unsigned long long c_cnt = 0;
+      long long c_first = 0x7FFFFFFFFFFFFFFFll;
+      float c_maxd = 0.0f, c_maxsq = 0.0f;
+      double c_sq = 0.0, c_rsq = 0.0;
       if (row_ok) {
         const float al = p.alpha ? *p.alpha : 1.0f;
         const bool rnan = (FMT == EMU_FMT_NVFP4) && p.row_nan[m];
@@ -890,8 +899,42 @@ emul_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
             float y = (float)acc[j];
             if (p.alpha) y = __fmul_rn(y, al);
             if (FMT == EMU_FMT_NVFP4 && (rnan || p.col_nan[n])) y = __int_as_float(0x7FFFFFFF);
-            store_output(p.out, m * p.N + n, y, p.out_mode);
+            if (!CMP || p.write_out) store_output(p.out, m * p.N + n, y, p.out_mode);
+            if (CMP) {
+              const float o = output_value(y, p.out_mode), r = load_output(p.cmp_ref, m * p.N + n, p.out_mode);
+              const float d = __fsub_rn(r, o);
+              if (!(r == o) && !((r != r) && (o != o))) {
+                ++c_cnt;
+                c_first = min(c_first, (long long)(m * p.N + n));
+                c_maxd = fmaxf(c_maxd, (d != d) ? __int_as_float(0x7F800000) : fabsf(d));
+              }
+              const float e2 = __fmul_rn(d, d), r2 = __fmul_rn(r, r);
+              if ((__float_as_uint(e2) & 0x7F800000u) != 0x7F800000u) { c_sq += (double)e2; c_maxsq = fmaxf(c_maxsq, e2); }
+              if ((__float_as_uint(r2) & 0x7F800000u) != 0x7F800000u) c_rsq += (double)r2;
+            }
           }
+        }
+      }
+      if (CMP) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+          c_cnt += __shfl_xor_sync(0xFFFFFFFFu, c_cnt, o);
+          c_first = min(c_first, __shfl_xor_sync(0xFFFFFFFFu, c_first, o));
+          c_maxd = fmaxf(c_maxd, __shfl_xor_sync(0xFFFFFFFFu, c_maxd, o));
+          c_maxsq = fmaxf(c_maxsq, __shfl_xor_sync(0xFFFFFFFFu, c_maxsq, o));
+          c_sq += __shfl_xor_sync(0xFFFFFFFFu, c_sq, o);
+          c_rsq += __shfl_xor_sync(0xFFFFFFFFu, c_rsq, o);
+        }
+        if (lane == 0) {
+          emu_compare_stats* st = p.cmp_stats;
+          if (c_cnt) {
+            atomicAdd(reinterpret_cast<unsigned long long*>(&st->mismatches), c_cnt);
+            atomicMin(reinterpret_cast<long long*>(&st->first_index), c_first);
+            atomicMax(reinterpret_cast<unsigned int*>(&st->max_diff), __float_as_uint(c_maxd));
+          }
+          atomicMax(reinterpret_cast<unsigned int*>(&st->max_sq_error), __float_as_uint(c_maxsq));
+          atomicAdd(&st->sq_error_sum, c_sq);
+          atomicAdd(&st->ref_sq_sum, c_rsq);
         }
       }
     }
@@ -1071,6 +1114,9 @@ static cudaError_t run_tc(const uint8_t* A, const uint8_t* B, const uint8_t* SA,
   prm.r3 = args.stage3_rounding;
   prm.r4 = args.stage4_rounding;
   prm.out_mode = args.out_mode;
+  prm.cmp_ref = args.cmp_ref;
+  prm.cmp_stats = args.cmp_stats;
+  prm.write_out = args.write_out ? 1 : 0;
 
   const unsigned grid = (unsigned)std::min<int64_t>(tiles_m * tiles_n, sms);
   const int rm = nb == 1 ? args.stage3_rounding : args.stage4_rounding;
@@ -1080,8 +1126,12 @@ static cudaError_t run_tc(const uint8_t* A, const uint8_t* B, const uint8_t* SA,
     kern<<<grid, threads, SMEM_BYTES, stream>>>(tmA, tmB, tmAF, tmBF, prm);
     return cudaSuccess;
   };
-  e = rm == EMU_RNE ? launch(emul_gemm_tc_kernel<FMT, EMU_RNE>, 32 * NUM_WARPS)
-                    : launch(emul_gemm_tc_kernel<FMT, EMU_RZ>, 32 * NUM_WARPS);
+  if (args.cmp_ref)
+    e = rm == EMU_RNE ? launch(emul_gemm_tc_kernel<FMT, EMU_RNE, true>, 32 * NUM_WARPS)
+                      : launch(emul_gemm_tc_kernel<FMT, EMU_RZ, true>, 32 * NUM_WARPS);
+  else
+    e = rm == EMU_RNE ? launch(emul_gemm_tc_kernel<FMT, EMU_RNE, false>, 32 * NUM_WARPS)
+                      : launch(emul_gemm_tc_kernel<FMT, EMU_RZ, false>, 32 * NUM_WARPS);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }

@@ -13,6 +13,10 @@ struct GemmArgs {
   int stage3_rounding;  // EMU_RZ / EMU_RNE
   int stage4_rounding;
   int out_mode;         // EMU_OUT_*
+  // optional comparison of the result with a reference output, fused into the tensor-core epilogue
+  const void* cmp_ref = nullptr;          // [M][N], the output's dtype
+  emu_compare_stats* cmp_stats = nullptr; // device; initialised by launch_compare_init
+  bool write_out = true;                  // false: compare only, `out` is not written
 };
 
 cudaError_t launch_gemm_simt(const uint8_t* A, const uint8_t* B, const uint8_t* SA, const uint8_t* SB,
@@ -36,6 +40,8 @@ cudaError_t launch_global_scales(const void* a, int64_t a_numel, const void* b, 
                                  int dtype, float* gs_a, float* gs_b, float* alpha,
                                  cudaStream_t stream);
 
+cudaError_t launch_compare_init(emu_compare_stats* stats, int64_t n, cudaStream_t stream);
+cudaError_t launch_compare_fini(emu_compare_stats* stats, cudaStream_t stream);
 cudaError_t launch_compare(const void* ref, const void* out, int dtype, int64_t n, emu_compare_stats* stats,
                            cudaStream_t stream);
 cudaError_t launch_dequant(const uint8_t* q, const uint8_t* sf, int64_t rows, int64_t K, int64_t sf_cols, int fmt,

@@ -202,6 +202,22 @@ EMU_API emu_status emu_compare(const void* ref, const void* out, int32_t dtype, 
                                emu_compare_stats* stats, void* stream);
 
 /*
+ * emu_gemm_ws fused with emu_compare: the emulated GEMM's output compared on the device with `ref`
+ * ([M][N], the output's dtype), filling `stats` as emu_compare(ref, out) does (the squared-error sums
+ * accumulate in another order, so they agree to rounding).  On the tensor-core path (workspace given
+ * and the shape taken) the comparison runs in the GEMM epilogue and `out` may be NULL, in which
+ * case no output is written; otherwise the CUDA-core GEMM writes `out` (then required) and
+ * emu_compare runs after it.  This is the mismatch count of gemm_compare's runner
+ * (gemm_compare/runner.py:20-79 applied to emul_fn's output) without the M x N round trip.
+ */
+EMU_API emu_status emu_gemm_compare(const uint8_t* a_fp4, const uint8_t* b_fp4, const uint8_t* scale_a,
+                                    const uint8_t* scale_b, int64_t M, int64_t N, int64_t K,
+                                    int64_t scale_a_rows, int64_t scale_a_cols, int64_t scale_b_rows,
+                                    int64_t scale_b_cols, const float* alpha, const emu_gemm_params* params,
+                                    const void* ref, void* out, emu_compare_stats* stats, void* workspace,
+                                    size_t workspace_bytes, void* stream);
+
+/*
  * Dequantise packed FP4 to f32: out[r][k] = e2m1(q[r][k]) * scale(r, k / group), scales in the
  * swizzled layout ([pad128(rows)][sf_cols]).  MXFP4: scale = f32 with bits (u << 23) (u = 0 -> 0,
  * u = 255 -> inf), as flashinfer.mxfp4_dequantize, the reference's MXFP4 pseudo_fn operand

@@ -167,3 +167,36 @@ def test_replay_through_emulated_gemm(tmp_path):
     del cases[1]
     rollout.save_rollout_artifact(p, backend="nvfp", meta={}, seed=0, cases=cases)
     assert replay.run_suite_import(emul_fn, backend="nvfp", artifact_path=p) == 0
+
+
+@pytest.mark.parametrize("kind,out_mode", [("nvfp", 0), ("mxfp", 1), ("nvfp", 2)])
+def test_fused_gemm_compare_matches_separate_compare(kind, out_mode):
+    """emu_gemm_compare (comparison in the tensor-core epilogue) against emu_gemm_ws + emu_compare."""
+    from emugen_b200 import _lib
+    from tests.golden.make_golden import gen_inputs
+
+    case = dict(kind=kind, data="outliers", M=256, N=192, K=1024)
+    a, b, sfa, sfb, alpha = gen_inputs(case, np.random.default_rng(21))
+    t = [torch.from_numpy(np.ascontiguousarray(x)).cuda() for x in (a, b, sfa, sfb)]
+    kw = dict(fmt=0 if kind == "nvfp" else 1, group_size=16 if kind == "nvfp" else 32,
+              w_reduce=4 if kind == "nvfp" else 2, stage3_rounding=0, stage4_rounding=0,
+              alpha=torch.tensor([float(alpha)], device="cuda") if kind == "nvfp" else None, out_mode=out_mode)
+    out = _lib.gemm(*t, **kw)
+    ref = out.clone()
+    flat = ref.view(-1)
+    flat[7] = flat[7] * 2 + 1
+    flat[1000] = float("nan")
+    flat[5000] = -flat[5000] if flat[5000] != 0 else 1.0
+    for path in ("auto", "simt"):
+        for write_out in (False, True):
+            st, o = _lib.gemm_compare(*t, ref, path=path, write_out=write_out, **kw)
+            want = _lib.compare_stats(ref, out)
+            for k in ("mismatches", "first_index", "max_diff", "max_sq_error", "numel"):
+                assert st[k] == want[k], (path, write_out, k, st[k], want[k])
+            for k in ("sq_error_sum", "ref_sq_sum"):
+                assert math.isclose(st[k], want[k], rel_tol=1e-12), (k, st[k], want[k])
+            if o is not None:
+                assert torch.equal(o.view(torch.int16) if o.dtype != torch.float32 else o.view(torch.int32),
+                                   out.view(torch.int16) if out.dtype != torch.float32 else out.view(torch.int32))
+    st, _ = _lib.gemm_compare(*t, out, **kw)
+    assert st["mismatches"] == 0 and st["first_index"] == -1 and st["max_diff"] == 0
