@@ -26,7 +26,7 @@ ABI_VERSION = 1
 
 SYMBOLS = ("emu_abi_version", "emu_last_error", "emu_status_string", "emu_gemm", "emu_gemm_workspace_size",
            "emu_gemm_ws", "emu_gemm_static", "emu_nvfp4_global_scales", "emu_quant_nvfp4", "emu_quant_mxfp4",
-           "emu_gemm_compare", "emu_compare", "emu_dequant_fp4")
+           "emu_gemm_model", "emu_gemm_compare", "emu_compare", "emu_dequant_fp4")
 STATIC_SCRATCH_BYTES = 64 << 20   # EMU_STATIC_SCRATCH_BYTES
 
 
@@ -40,6 +40,11 @@ class EmuCompareStats(ctypes.Structure):
     _fields_ = [("mismatches", ctypes.c_int64), ("first_index", ctypes.c_int64), ("max_diff", ctypes.c_float),
                 ("max_sq_error", ctypes.c_float), ("sq_error_sum", ctypes.c_double), ("ref_sq_sum", ctypes.c_double),
                 ("numel", ctypes.c_int64)]
+
+
+class EmuAccumModel(ctypes.Structure):
+    _fields_ = [("align3", ctypes.c_int32), ("align4", ctypes.c_int32), ("align_rounding", ctypes.c_int32),
+                ("order", ctypes.c_int32)]
 
 
 class EmuError(RuntimeError):
@@ -89,6 +94,9 @@ def load() -> ctypes.CDLL:
         L.emu_quant_nvfp4.argtypes = [vp, i32, i64, i64, vp, vp, vp, vp]
         L.emu_quant_mxfp4.restype = i32
         L.emu_quant_mxfp4.argtypes = [vp, i32, i64, i64, vp, vp, vp]
+        L.emu_gemm_model.restype = i32
+        L.emu_gemm_model.argtypes = [vp, vp, vp, vp, i64, i64, i64, i64, i64, i64, i64, vp,
+                                     ctypes.POINTER(EmuGemmParams), ctypes.POINTER(EmuAccumModel), vp, vp]
         L.emu_gemm_compare.restype = i32
         L.emu_gemm_compare.argtypes = [vp, vp, vp, vp, i64, i64, i64, i64, i64, i64, i64, vp,
                                        ctypes.POINTER(EmuGemmParams), vp, vp, vp, vp, ctypes.c_size_t, vp]
@@ -322,3 +330,30 @@ def gemm_compare(a_fp4: torch.Tensor, b_fp4: torch.Tensor, scale_a: torch.Tensor
     _check(status)
     host = EmuCompareStats.from_buffer_copy(bytes(st.cpu().numpy()))
     return {k: getattr(host, k) for k, _ in EmuCompareStats._fields_}, out
+
+
+def gemm_model(a_fp4: torch.Tensor, b_fp4: torch.Tensor, scale_a: torch.Tensor, scale_b: torch.Tensor, *,
+               fmt: int, group_size: int, w_reduce: int, stage3_rounding: int, stage4_rounding: int,
+               alpha: torch.Tensor | None, out_mode: int, align3: int = 0, align4: int = 0,
+               align_rounding: int = EMU_RZ, order: int = 0) -> torch.Tensor:
+    """Emulated GEMM under an accumulator model (emu_gemm_model); all-zero model = gemm()."""
+    L = load()
+    on_cpu = not any(t.is_cuda for t in (a_fp4, b_fp4, scale_a, scale_b))
+    dev = _device_for(a_fp4, b_fp4, scale_a, scale_b)
+    M, N, K = a_fp4.shape[0], b_fp4.shape[0], a_fp4.shape[1] * 2
+    a = _bytes2d(a_fp4, dev, "a_fp4")
+    b = _bytes2d(b_fp4, dev, "b_fp4")
+    sa = _bytes2d(scale_a, dev, "scale_a")
+    sb = _bytes2d(scale_b, dev, "scale_b")
+    al = None if alpha is None else alpha.detach().reshape(1).to(device=dev, dtype=torch.float32).contiguous()
+    odt = {EMU_OUT_F16: torch.float16, EMU_OUT_BF16_VIA_F16: torch.bfloat16, EMU_OUT_F32: torch.float32}[out_mode]
+    out = torch.empty((M, N), dtype=odt, device=dev)
+    params = EmuGemmParams(fmt, group_size, w_reduce, stage3_rounding, stage4_rounding, out_mode)
+    model = EmuAccumModel(align3, align4, align_rounding, order)
+    with torch.cuda.device(dev):
+        status = L.emu_gemm_model(a.data_ptr(), b.data_ptr(), sa.data_ptr(), sb.data_ptr(), M, N, K,
+                                  sa.shape[0], sa.shape[1], sb.shape[0], sb.shape[1],
+                                  None if al is None else al.data_ptr(), ctypes.byref(params), ctypes.byref(model),
+                                  out.data_ptr(), _stream(dev))
+    _check(status)
+    return out.cpu() if on_cpu else out

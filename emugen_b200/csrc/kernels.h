@@ -19,6 +19,15 @@ struct GemmArgs {
   bool write_out = true;                  // false: compare only, `out` is not written
 };
 
+// Accumulator model of emu_gemm_model (include/emugen.h emu_accum_model).
+struct ModelArgs {
+  int align3, align4, align_rounding, order;
+};
+
+cudaError_t launch_gemm_model(const uint8_t* A, const uint8_t* B, const uint8_t* SA, const uint8_t* SB, int64_t M,
+                              int64_t N, int64_t K, int64_t sa_cols, int64_t sb_cols, const float* alpha,
+                              const GemmArgs& args, const ModelArgs& ma, void* out, cudaStream_t stream);
+
 cudaError_t launch_gemm_simt(const uint8_t* A, const uint8_t* B, const uint8_t* SA, const uint8_t* SB,
                              int64_t M, int64_t N, int64_t K, int64_t sa_cols, int64_t sb_cols,
                              const float* alpha, const GemmArgs& args, void* out, cudaStream_t stream);

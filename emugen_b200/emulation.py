@@ -208,6 +208,35 @@ def emulated_fp4_mm(a, b, block_scale_a, block_scale_b, alpha, out_dtype=torch.f
 
 emulated_scaled_fp4_mm = emulated_fp4_mm
 
+
+@dataclass(frozen=True)
+class AccumModel:
+    """Accumulator model for sweeps (no reference counterpart: the reference accepts w_stage3 /
+    w_stage4 and ignores them, core.py:31-38).  align3 / align4: alignment widths of stage 3 /
+    stage 4 (0 = exact, the reference); align_rounding: RoundStrategy.RZ truncates the aligned
+    addends, RNE rounds them to nearest even; order: stage-3 f64 order when align3 == 0
+    (0 left to right = reference, 1 right to left, 2 pairwise tree).  Semantics in include/emugen.h."""
+    align3: int = 0
+    align4: int = 0
+    align_rounding: RoundStrategy | int = RoundStrategy.RZ
+    order: int = 0
+
+
+def emulate_with_model(state, model: AccumModel) -> torch.Tensor:
+    """``emulate_nvfp_scaled_fp4_mm(state)`` under ``model`` (all-zero model = identical results)."""
+    od = state.out_dtype
+    out_mode = _lib.EMU_OUT_BF16_VIA_F16 if od == torch.bfloat16 else _lib.EMU_OUT_F16
+    gs = int(state.group_size)
+    if gs not in (16, 32):
+        raise NotImplementedError(f"group_size {gs}: only 16 (NVFP4) and 32 (MXFP4) are supported")
+    out = _lib.gemm_model(state.a_fp4, state.b_fp4, state.scale_a, state.scale_b,
+                          fmt=_lib.EMU_FMT_NVFP4 if gs == 16 else _lib.EMU_FMT_MXFP4, group_size=gs,
+                          w_reduce=int(state.w_reduce), stage3_rounding=_rounding_code(state.stage3_rounding),
+                          stage4_rounding=_rounding_code(state.stage4_rounding), alpha=state.alpha,
+                          out_mode=out_mode, align3=int(model.align3), align4=int(model.align4),
+                          align_rounding=_rounding_code(model.align_rounding), order=int(model.order))
+    return out if out.dtype == od else out.to(od)
+
 __all__ = ["RoundStrategy", "coerce_round_strategy", "HardwareConfig", "CONFIG_RTX_5090", "MMAEngine",
            "SearchNVFPEmulationState", "emulate_nvfp_scaled_fp4_mm", "EmulationKernel", "emulated_fp4_mm",
-           "emulated_scaled_fp4_mm"]
+           "emulated_scaled_fp4_mm", "AccumModel", "emulate_with_model"]

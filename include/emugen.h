@@ -123,6 +123,37 @@ EMU_API emu_status emu_gemm_ws(const uint8_t* a_fp4, const uint8_t* b_fp4, const
                        void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * Accumulator model beyond the reference.  The reference keeps w_stage3 / w_stage4 as parameters
+ * and ignores them (search/emulation/core.py:31-38, config.py:16-19); this model gives them a
+ * definition, for on-device parameter sweeps (no reference oracle exists for nonzero values):
+ *   align3 (W3, 0 or 1..46): stage 3 aligns the block's addends to the largest exponent E among the
+ *           finite nonzero ones, each rounded (align_rounding: EMU_RZ truncate, EMU_RNE) onto the
+ *           grid 2^(E - W3 + 1), then sums them exactly; a non-finite addend leaves the f64 sum.
+ *   align4 (W4, 0 or 1..52): stage 4 aligns acc and the block sum the same way before R4.
+ *   order (0..2), used when align3 == 0: stage-3 f64 summation order, 0 left to right (the
+ *           reference), 1 right to left, 2 pairwise tree.
+ * All zero = the reference model.
+ */
+typedef struct emu_accum_model {
+  int32_t align3;
+  int32_t align4;
+  int32_t align_rounding;
+  int32_t order;
+} emu_accum_model;
+
+/*
+ * emu_gemm under an accumulator model.  A zero model runs emu_gemm itself.  A nonzero model runs a
+ * CUDA-core kernel that needs w_reduce <= 16.  Replaces the reference's HardwareConfig-driven
+ * MMAEngine.emulation_scaled_fp4_mm (search/emulation/core.py:69-148) for sweeps over the fields
+ * the reference leaves unimplemented.
+ */
+EMU_API emu_status emu_gemm_model(const uint8_t* a_fp4, const uint8_t* b_fp4, const uint8_t* scale_a,
+                                  const uint8_t* scale_b, int64_t M, int64_t N, int64_t K,
+                                  int64_t scale_a_rows, int64_t scale_a_cols, int64_t scale_b_rows,
+                                  int64_t scale_b_cols, const float* alpha, const emu_gemm_params* params,
+                                  const emu_accum_model* model, void* out, void* stream);
+
+/*
  * Bytes of the per-device static scratch behind emu_gemm_static (64 MiB).
  */
 #define EMU_STATIC_SCRATCH_BYTES (64u << 20)

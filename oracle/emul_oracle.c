@@ -119,6 +119,21 @@ static int64_t swz_index(int64_t r, int64_t c, int64_t cols_pad) {
   return (r / 128) * (kt * 512) + (c / 4) * 512 + (r % 32) * 16 + ((r % 128) / 32) * 4 + (c % 4);
 }
 
+/*
+ * Accumulator model beyond the reference (its w_stage3 / w_stage4 are accepted and unused,
+ * search/emulation/core.py:31-38, config.py:16-19).  This build defines them as follows; with all
+ * fields 0 the model is exactly the reference's.  No reference oracle exists for nonzero fields.
+ *   align3 = W3 > 0: stage 3 aligns the block's addends v_g to the largest exponent E among the
+ *            finite nonzero ones: each becomes round(v_g / q) * q, q = 2^(E - W3 + 1), with
+ *            align_rm (RZ: truncate toward zero, RNE: nearest even); the rounded addends are summed
+ *            exactly.  A non-finite addend makes the sum the plain f64 sum (inf / NaN as IEEE).
+ *   align4 = W4 > 0: stage 4 aligns acc and s_b the same way (to the larger of their exponents),
+ *            sums them exactly, then rounds to f32 with R4 (the first block aligns s_0 alone; a
+ *            single-block GEMM has no stage 4 and rounds s_0 with R3 as the reference does).
+ *   Limits: w_reduce <= 64, W3 <= 46, W4 <= 52 keep every aligned sum exact in f64.
+ *   order:   stage-3 summation order when align3 == 0: 0 left to right (the reference), 1 right to
+ *            left, 2 pairwise tree (adjacent pairs, then pairs of pairs, ...); all start from +0.0.
+ */
 struct job {
   const int8_t *ua, *ub;
   const float *sa, *sb;
@@ -128,7 +143,70 @@ struct job {
   int out_mode;
   void* out;
   int t, nt;
+  int align3, align4, align_rm, order;
 };
+
+/* floor(log2 |x|) of a finite nonzero double. */
+static int exp_of(double x) {
+  int e;
+  frexp(x, &e);
+  return e - 1;
+}
+
+/* x / q rounded to an integer (q a power of two, |x / q| < 2^62), RZ or RNE. */
+static int64_t round_to_grid(double x, int e_q, int rm) {
+  double y = ldexp(x, -e_q); /* exact */
+  double r = rm == OR_RZ ? trunc(y) : nearbyint(y); /* nearbyint: current mode, round-to-nearest-even */
+  return (int64_t)r;
+}
+
+/* Stage 3 under the model: the block sum of v[0..n-1]. */
+static double model_stage3(const double* v, int n, int align, int rm, int order) {
+  int finite = 1;
+  for (int i = 0; i < n; ++i) finite &= isfinite(v[i]) ? 1 : 0;
+  if (align > 0 && finite) {
+    int have = 0, E = 0;
+    for (int i = 0; i < n; ++i)
+      if (v[i] != 0.0) { int e = exp_of(v[i]); if (!have || e > E) E = e; have = 1; }
+    if (!have) return 0.0;
+    const int eq = E - align + 1;
+    int64_t m = 0;
+    for (int i = 0; i < n; ++i) m += round_to_grid(v[i], eq, rm);
+    return ldexp((double)m, eq) + 0.0; /* + 0.0: an exact zero sum is +0 */
+  }
+  if (order == 1) {
+    double s = 0.0;
+    for (int i = n - 1; i >= 0; --i) s = s + v[i];
+    return s;
+  }
+  if (order == 2) {
+    double t[64];
+    int k = n;
+    for (int i = 0; i < n; ++i) t[i] = v[i];
+    while (k > 1) {
+      int h = 0;
+      for (int i = 0; i + 1 < k; i += 2) t[h++] = t[i] + t[i + 1];
+      if (k & 1) t[h++] = t[k - 1];
+      k = h;
+    }
+    return 0.0 + t[0];
+  }
+  double s = 0.0;
+  for (int i = 0; i < n; ++i) s = s + v[i];
+  return s;
+}
+
+/* Stage 4 under the model: acc + s before the R4 rounding (acc == 0 for the first block). */
+static double model_stage4_sum(double acc, double s, int align, int rm) {
+  if (align <= 0 || !isfinite(acc) || !isfinite(s)) return acc + s;
+  int have = 0, E = 0;
+  if (acc != 0.0) { E = exp_of(acc); have = 1; }
+  if (s != 0.0) { int e = exp_of(s); if (!have || e > E) E = e; have = 1; }
+  if (!have) return acc + s;
+  const int eq = E - align + 1;
+  const int64_t m = round_to_grid(acc, eq, rm) + round_to_grid(s, eq, rm);
+  return ldexp((double)m, eq) + 0.0;
+}
 
 /* Rows t, t+nt, t+2nt, ... of the output. */
 static void* run_rows(void* arg) {
@@ -141,7 +219,7 @@ static void* run_rows(void* arg) {
       const int8_t* rb = j->ub + n * K;
       float acc = 0.0f;
       for (int64_t blk = 0; blk < nb; ++blk) {
-        double s = 0.0; /* stage 3 starts from +0.0 */
+        double vals[64];
         for (int w = 0; w < w_reduce; ++w) {
           int64_t g = blk * w_reduce + w;
           int dot4 = 0; /* exact group dot product times 4 */
@@ -158,11 +236,13 @@ static void* run_rows(void* arg) {
             float vf = p * c;
             v = (double)vf;
           }
-          s = s + v;
+          vals[w] = v;
         }
+        /* stage 3 (the reference: ((+0.0 + v0) + v1) + ..., left to right in f64) */
+        const double s = model_stage3(vals, w_reduce, j->align3, j->align_rm, j->order);
         if (nb == 1) acc = round_f64_to_f32(s, j->r3);
-        else if (blk == 0) acc = round_f64_to_f32(s, j->r4);
-        else acc = round_f64_to_f32((double)acc + s, j->r4);
+        else if (blk == 0) acc = round_f64_to_f32(model_stage4_sum(0.0, s, j->align4, j->align_rm), j->r4);
+        else acc = round_f64_to_f32(model_stage4_sum((double)acc, s, j->align4, j->align_rm), j->r4);
       }
       float y = acc;
       if (j->alpha) y = acc * j->alpha[0];
@@ -186,12 +266,13 @@ static void* run_rows(void* arg) {
  *   out       uint16 bits for OR_OUT_F16 / OR_OUT_BF16_VIA_F16, float for OR_OUT_F32
  * Returns 0 on success, a negative code for an argument the reference rejects.
  */
-int oracle_emul_gemm(const uint8_t* a, const uint8_t* b, const uint8_t* sfa, const uint8_t* sfb,
-                     int64_t M, int64_t N, int64_t K, int64_t sfa_rows, int64_t sfa_cols,
-                     int64_t sfb_rows, int64_t sfb_cols, int scale_fmt, int group_size,
-                     int w_reduce, int r3, int r4, const float* alpha, int out_mode, void* out,
-                     int nthreads) {
+int oracle_emul_gemm_model(const uint8_t* a, const uint8_t* b, const uint8_t* sfa, const uint8_t* sfb,
+                           int64_t M, int64_t N, int64_t K, int64_t sfa_rows, int64_t sfa_cols,
+                           int64_t sfb_rows, int64_t sfb_cols, int scale_fmt, int group_size,
+                           int w_reduce, int r3, int r4, const float* alpha, int out_mode, void* out,
+                           int nthreads, int align3, int align4, int align_rm, int order) {
   if (group_size != 16 && group_size != 32) return -1;
+  if (w_reduce > 64 || align3 < 0 || align3 > 46 || align4 < 0 || align4 > 52 || order < 0 || order > 2) return -7;
   if (K % group_size != 0) return -2;
   const int64_t G = K / group_size;
   if (w_reduce <= 0 || G % w_reduce != 0) return -3;
@@ -233,7 +314,7 @@ int oracle_emul_gemm(const uint8_t* a, const uint8_t* b, const uint8_t* sfa, con
 
   {
     struct job j = {ua, ub, sa, sb, M, N, K, G, nb, group_size, w_reduce, r3, r4, f64_combine,
-                    alpha, out_mode, out, 0, 1};
+                    alpha, out_mode, out, 0, 1, align3, align4, align_rm, order};
     int nt = nthreads > 0 ? nthreads : 1;
     if (nt > 256) nt = 256;
     if (nt > M) nt = M > 0 ? (int)M : 1;
@@ -246,6 +327,15 @@ int oracle_emul_gemm(const uint8_t* a, const uint8_t* b, const uint8_t* sfa, con
   }
   free(ua); free(ub); free(sa); free(sb);
   return 0;
+}
+
+int oracle_emul_gemm(const uint8_t* a, const uint8_t* b, const uint8_t* sfa, const uint8_t* sfb,
+                     int64_t M, int64_t N, int64_t K, int64_t sfa_rows, int64_t sfa_cols,
+                     int64_t sfb_rows, int64_t sfb_cols, int scale_fmt, int group_size,
+                     int w_reduce, int r3, int r4, const float* alpha, int out_mode, void* out,
+                     int nthreads) {
+  return oracle_emul_gemm_model(a, b, sfa, sfb, M, N, K, sfa_rows, sfa_cols, sfb_rows, sfb_cols, scale_fmt,
+                                group_size, w_reduce, r3, r4, alpha, out_mode, out, nthreads, 0, 0, 0, 0);
 }
 
 /* Swizzled scale byte offset, exported so tests can build scale buffers. */

@@ -36,6 +36,8 @@ def lib() -> ctypes.CDLL:
         L.oracle_emul_gemm.restype = ctypes.c_int
         L.oracle_emul_gemm.argtypes = [ctypes.c_void_p] * 4 + [ctypes.c_int64] * 7 + [ctypes.c_int] * 5 + [
             ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_int]
+        L.oracle_emul_gemm_model.restype = ctypes.c_int
+        L.oracle_emul_gemm_model.argtypes = L.oracle_emul_gemm.argtypes + [ctypes.c_int] * 4
         L.oracle_swizzle_offset.restype = ctypes.c_int64
         L.oracle_swizzle_offset.argtypes = [ctypes.c_int64] * 3
         _lib = L
@@ -47,8 +49,10 @@ def _ptr(a: np.ndarray) -> int:
 
 
 def emul_gemm(a_fp4, b_fp4, sfa, sfb, *, scale_fmt, group_size, w_reduce, r3=RZ, r4=RZ,
-              alpha=None, out_mode=OUT_F16, nthreads=None) -> np.ndarray:
-    """Oracle emulated GEMM on numpy arrays.  Returns uint16 bits (f16 / bf16) or float32."""
+              alpha=None, out_mode=OUT_F16, nthreads=None, align3=0, align4=0, align_rm=RZ,
+              order=0) -> np.ndarray:
+    """Oracle emulated GEMM on numpy arrays.  Returns uint16 bits (f16 / bf16) or float32.
+    align3 / align4 / align_rm / order select the accumulator model (all 0: the reference's)."""
     a = np.ascontiguousarray(a_fp4, dtype=np.uint8)
     b = np.ascontiguousarray(b_fp4, dtype=np.uint8)
     sa = np.ascontiguousarray(sfa).view(np.uint8)
@@ -58,9 +62,10 @@ def emul_gemm(a_fp4, b_fp4, sfa, sfb, *, scale_fmt, group_size, w_reduce, r3=RZ,
     out = np.empty((M, N), dtype=np.float32 if out_mode == OUT_F32 else np.uint16)
     al = None if alpha is None else np.array([alpha], dtype=np.float32)
     nt = nthreads or os.cpu_count() or 1
-    rc = lib().oracle_emul_gemm(_ptr(a), _ptr(b), _ptr(sa), _ptr(sb), M, N, K, sa.shape[0], sa.shape[1],
-                                sb.shape[0], sb.shape[1], scale_fmt, group_size, w_reduce, r3, r4,
-                                None if al is None else _ptr(al), out_mode, _ptr(out), nt)
+    rc = lib().oracle_emul_gemm_model(_ptr(a), _ptr(b), _ptr(sa), _ptr(sb), M, N, K, sa.shape[0], sa.shape[1],
+                                      sb.shape[0], sb.shape[1], scale_fmt, group_size, w_reduce, r3, r4,
+                                      None if al is None else _ptr(al), out_mode, _ptr(out), nt,
+                                      align3, align4, align_rm, order)
     if rc != 0:
         raise ValueError(f"oracle rejected arguments (code {rc})")
     return out
