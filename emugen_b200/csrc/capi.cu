@@ -145,6 +145,10 @@ emu_status emu_gemm_ws(const uint8_t* a_fp4, const uint8_t* b_fp4, const uint8_t
                                            args, out, workspace, s),
                        "emu_gemm tensor-core launch");
   }
+  if (emu::gemm_skinny_supported(M, K) && M < 128)
+    return cuda_status(emu::launch_gemm_skinny(a_fp4, b_fp4, scale_a, scale_b, M, N, K, scale_a_cols, scale_b_cols,
+                                               alpha, args, out, s),
+                       "emu_gemm skinny launch");
   return cuda_status(emu::launch_gemm_simt(a_fp4, b_fp4, scale_a, scale_b, M, N, K, scale_a_cols, scale_b_cols, alpha,
                                            args, out, s),
                      "emu_gemm launch");
