@@ -1,5 +1,5 @@
 // Thin inline-PTX wrappers for the sm_100a features the tensor-core kernel uses: mbarriers with
-// bounded waits, TMA tile loads (no multicast), tcgen05 MMA / TMEM alloc, load and fences.
+// bounded waits, TMA tile loads into this CTA only, tcgen05 MMA / TMEM alloc, load and fences.
 #pragma once
 
 #include <cuda.h>
@@ -61,7 +61,7 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
-// Non-tensor bulk copy global -> shared (16-byte aligned, size a multiple of 16), no multicast.
+// Non-tensor bulk copy global -> this CTA's shared memory (16-byte aligned, size a multiple of 16).
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
                ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
