@@ -200,3 +200,16 @@ def test_fused_gemm_compare_matches_separate_compare(kind, out_mode):
                                    out.view(torch.int16) if out.dtype != torch.float32 else out.view(torch.int32))
     st, _ = _lib.gemm_compare(*t, out, **kw)
     assert st["mismatches"] == 0 and st["first_index"] == -1 and st["max_diff"] == 0
+
+
+def test_suite_on_device_emul_vs_emul():
+    """run_suite with the emulation as both sides (must match exactly) and the pseudo GEMM as the
+    'real' side in MSE mode, on the GPU with the on-device comparison."""
+    from emugen_b200 import suite
+    from emugen_b200.backends.mxfp import build_mxfp_fns
+
+    quant_fn, _real, emul_fn, pseudo_fn, _meta = build_mxfp_fns(return_pseudo=True)
+    kw = dict(num_iterations=4, dims_m=[128, 256], dims_n=[64, 128], dims_k=[256, 512],
+              distributions=["normal", "student_t", "outliers"], seed=3)
+    assert suite.run_suite(quant_fn, emul_fn, emul_fn, **kw) == 0
+    assert suite.run_suite(quant_fn, lambda s: pseudo_fn(s).to(torch.float16), emul_fn, metric_mode="mse", **kw) == 0
