@@ -145,7 +145,7 @@ emu_status emu_gemm_ws(const uint8_t* a_fp4, const uint8_t* b_fp4, const uint8_t
                                            args, out, workspace, s),
                        "emu_gemm tensor-core launch");
   }
-  if (emu::gemm_skinny_supported(M, K) && M < 128)
+  if (emu::gemm_skinny_supported(p.format, p.w_reduce, M))
     return cuda_status(emu::launch_gemm_skinny(a_fp4, b_fp4, scale_a, scale_b, M, N, K, scale_a_cols, scale_b_cols,
                                                alpha, args, out, s),
                        "emu_gemm skinny launch");

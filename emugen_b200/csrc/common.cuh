@@ -24,6 +24,19 @@ __host__ __device__ __forceinline__ int e2m1_twice(uint32_t code) {
   return (code & 8u) ? -v : v;
 }
 
+// Four e2m1 codes (bits 0-15, code i in bits 4i..4i+3) -> four int8 "2x" values, byte i = code i.
+// Two byte permutes look the magnitude up in a positive and a negated table, a third turns each sign
+// bit into a byte mask that picks between them (code 8, negative zero, gives 0).
+__device__ __forceinline__ uint32_t e2m1x4_to_int8x4(uint32_t codes) {
+  const uint32_t sel = codes & 0x7777u;
+  const uint32_t sel_sign = (codes >> 3) & 0x1111u;
+  uint32_t pos, neg, msk;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(pos) : "r"(0x03020100u), "r"(0x0C080604u), "r"(sel));
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(neg) : "r"(0xFDFEFF00u), "r"(0xF4F8FAFCu), "r"(sel));
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(msk) : "r"(0x0000FF00u), "r"(0u), "r"(sel_sign));
+  return (pos & ~msk) | (neg & msk);
+}
+
 // Byte offset of scale (row r, scale column c) in a swizzled 128x4 buffer whose column count is
 // cols_pad (a multiple of 4).  Reference un-swizzle: nvfp_emulation.cpp:24-26
 // (reshape (m_tiles, k_tiles, 32, 4, 4).transpose(1, 3)).

@@ -33,22 +33,8 @@ constexpr int ROW_WORDS = KC / 4 + 4;         // int8 row of the chunk + 16 byte
 
 // Expand 16 packed e2m1 nibbles (8 bytes) into 16 int8 values 2*x.
 __device__ __forceinline__ uint4 unpack16(uint2 w) {
-  uint32_t in[2] = {w.x, w.y};
-  uint32_t out[4];
-#pragma unroll
-  for (int h = 0; h < 2; ++h) {
-#pragma unroll
-    for (int q = 0; q < 2; ++q) {
-      uint32_t packed = 0;
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const uint32_t nib = (in[h] >> (4 * (4 * q + e))) & 0xFu;
-        packed |= ((uint32_t)(uint8_t)(int8_t)e2m1_twice(nib)) << (8 * e);
-      }
-      out[2 * h + q] = packed;
-    }
-  }
-  return make_uint4(out[0], out[1], out[2], out[3]);
+  return make_uint4(e2m1x4_to_int8x4(w.x & 0xFFFFu), e2m1x4_to_int8x4(w.x >> 16), e2m1x4_to_int8x4(w.y & 0xFFFFu),
+                    e2m1x4_to_int8x4(w.y >> 16));
 }
 
 template <int FMT>

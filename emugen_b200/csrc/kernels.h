@@ -28,8 +28,8 @@ cudaError_t launch_gemm_model(const uint8_t* A, const uint8_t* B, const uint8_t*
                               int64_t N, int64_t K, int64_t sa_cols, int64_t sb_cols, const float* alpha,
                               const GemmArgs& args, const ModelArgs& ma, void* out, cudaStream_t stream);
 
-// Skinny problems (few rows of A): one thread per output column streaming B (gemm_skinny.cu).
-bool gemm_skinny_supported(int64_t M, int64_t K);
+// Skinny problems (M < 128): block sums split over warps, stage-4 chains per output (gemm_skinny.cu).
+bool gemm_skinny_supported(int fmt, int w_reduce, int64_t M);
 cudaError_t launch_gemm_skinny(const uint8_t* A, const uint8_t* B, const uint8_t* SA, const uint8_t* SB, int64_t M,
                                int64_t N, int64_t K, int64_t sa_cols, int64_t sb_cols, const float* alpha,
                                const GemmArgs& args, void* out, cudaStream_t stream);
