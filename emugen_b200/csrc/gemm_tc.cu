@@ -73,8 +73,10 @@ constexpr int CR_SBQ = 0, CR_KC = 1024, CR_CS = 1280, CR_SBW = 1792, CR_BYTES = 
 //   double2 rs[128]      row base {exponent word of 2^(52+e) (high half), (2^52 + 2^31) * 2^e}
 constexpr int RR_RS = 0, RR_BYTES = 2048;
 // Per-block path code (decide kernel): bits 0-1 the epilogue path, bit 2 set when the accumulator
-// provably stays in the f32 normal range (always for NVFP4), so 24-bit rounding in f64 is exact.
-constexpr uint8_t PATH_F64 = 0, PATH_INT = 1, PATH_SUM = 2, PATH_NORMAL = 4;
+// provably stays in the f32 normal range (always for NVFP4), so 24-bit rounding in f64 is exact;
+// bits 3-4 the group the mixed path keeps apart.
+constexpr uint8_t PATH_F64 = 0, PATH_INT = 1, PATH_SUM = 2, PATH_MIXED = 3, PATH_NORMAL = 4;
+constexpr int PATH_GROUP_SHIFT = 3;
 // Constant bias tiles for the block-sum path: A row r = {3072, 0, ...}, B row n = {4096, 0, ...} in
 // the 128-byte-swizzled K-major layout, so one K=16 MMA writes 3072 * 4096 = 1.5 * 2^23 everywhere.
 constexpr int BIAS_BYTES = A_BYTES + B_BYTES;
@@ -333,6 +335,21 @@ __global__ void col_tables_kernel(const uint8_t* __restrict__ sf, int64_t N, int
   }
 }
 
+// The group the mixed path keeps apart in a (column tile, K block): the one with the largest
+// max |2b| * |mb'| over the tile's columns (first on ties).  The fold kernel and the decide kernel both
+// derive it from the same table.
+template <int GPB>
+__device__ __forceinline__ int mixed_group(const float4* __restrict__ ctm, int64_t tn, int64_t kb, int64_t G) {
+  int gx = 0;
+  float best = ctm[tn * G + kb * GPB].y;
+#pragma unroll
+  for (int g = 1; g < GPB; ++g) {
+    const float v = ctm[tn * G + kb * GPB + g].y;
+    if (v > best) { best = v; gx = g; }
+  }
+  return gx;
+}
+
 // Block-sum path operands: the fp16 "2x" operand times its integer multiplier (ma * 2^(e_g - e) for A,
 // mb * 2^(e_g - e) for B).  Exact wherever the block passes the decide test (|product| <= 65504 and at
 // most 6 significant bits); other values are never read by that path.
@@ -355,16 +372,21 @@ __global__ void fold_rows_kernel(const __half* __restrict__ x16, int64_t rows, i
   }
 }
 
+// B operands: `out` every group folded (block-sum path); `out_mixed` (NVFP4) the same except the mixed
+// path's separate group of the (column tile, block), which keeps the plain "2x" values.
 template <int FMT>
 __global__ void fold_cols_kernel(const __half* __restrict__ x16, int64_t N, int64_t K, int64_t tiles_n,
-                                 const uint8_t* __restrict__ colrec, __half* __restrict__ out) {
+                                 const uint8_t* __restrict__ colrec, const float4* __restrict__ ctm,
+                                 __half* __restrict__ out, __half* __restrict__ out_mixed) {
   constexpr int GS = Fmt<FMT>::GS, GPB = Fmt<FMT>::GPB;
   const int64_t n8 = N * (K / 8);
+  const int64_t G = K / GS;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n8; i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t n = i / (K / 8), k0 = (i % (K / 8)) * 8;
     const int64_t g = k0 / GS, kb = g / GPB;
     const uint8_t* rec = colrec + (kb * tiles_n + n / BN) * CR_BYTES;
     const float m = (float)reinterpret_cast<const int32_t*>(rec + CR_SBQ)[(g % GPB) * BN + n % BN];
+    const bool apart = FMT == EMU_FMT_NVFP4 && (int)(g % GPB) == mixed_group<GPB>(ctm, n / BN, kb, G);
     const uint4 w = reinterpret_cast<const uint4*>(x16)[i];
     uint32_t in[4] = {w.x, w.y, w.z, w.w}, o[4];
 #pragma unroll
@@ -374,6 +396,7 @@ __global__ void fold_cols_kernel(const __half* __restrict__ x16, int64_t N, int6
       o[q] = *reinterpret_cast<const uint32_t*>(&h);
     }
     reinterpret_cast<uint4*>(out)[i] = make_uint4(o[0], o[1], o[2], o[3]);
+    if (FMT == EMU_FMT_NVFP4) reinterpret_cast<uint4*>(out_mixed)[i] = apart ? w : make_uint4(o[0], o[1], o[2], o[3]);
   }
 }
 
@@ -424,6 +447,9 @@ __global__ void tile_stats_kernel(int64_t rows, int64_t tile, int64_t ntiles, in
 //                   (max |x ma'| <= 65504); |T| < 2^31 for the int32 sum;
 //   block-sum path  additionally the folded B operand exact in fp16 and sum |x ma'| |y mb'| < 2^22
 //                   over the whole block, so the f32 accumulation of 1.5*2^23 + T is exact;
+//   mixed path      (NVFP4) the integer-path conditions, and the block-sum conditions over every group but
+//                   one (the column tile's group with the largest B multiplier), which gets its own
+//                   integer-path word;
 //   f64 path        every other block.
 template <int FMT>
 __global__ void decide_kernel(int64_t tiles_m, int64_t tiles_n, int64_t nb, int64_t G, PrepTables t) {
@@ -437,6 +463,10 @@ __global__ void decide_kernel(int64_t tiles_m, int64_t tiles_n, int64_t nb, int6
     bool ok = !t.rtinf[tm * nb + kb] && !t.ctinf[tn * nb + kb];
     bool fold_a = true, fold_b = true;
     double s1 = 0.0, s2 = 0.0, s3 = 0.0;
+    // the same sums without the mixed path's separate group
+    const int gx = mixed_group<GPB>(t.ctm, tn, kb, G);
+    bool fold_rest = true;
+    double r1 = 0.0, r2 = 0.0, r3 = 0.0;
 #pragma unroll
     for (int g = 0; g < GPB; ++g) {
       const int64_t gg = kb * GPB + g;
@@ -450,17 +480,30 @@ __global__ void decide_kernel(int64_t tiles_m, int64_t tiles_n, int64_t nb, int6
       ok = ok && p_small && (tmax < 4194304.0);
       // folded operands: max |2a * ma'| = max Linf * |ma'| (and the B side) must be exact fp16 values
       fold_a = fold_a && ((double)am.y * margin <= 65504.0);
-      fold_b = fold_b && ((double)bm.y * margin <= 65504.0);
-      s1 += (double)am.x * (double)bm.y * margin;
-      s2 += (double)am.y * (double)bm.x * margin;
-      s3 += sqrt((double)am.z * (double)bm.z) * margin * margin;
+      const bool fb = (double)bm.y * margin <= 65504.0;
+      fold_b = fold_b && fb;
+      const double t1 = (double)am.x * (double)bm.y * margin, t2 = (double)am.y * (double)bm.x * margin,
+                   t3 = sqrt((double)am.z * (double)bm.z) * margin * margin;
+      s1 += t1;
+      s2 += t2;
+      s3 += t3;
+      if (g != gx) {
+        fold_rest = fold_rest && fb;
+        r1 += t1;
+        r2 += t2;
+        r3 += t3;
+      }
     }
     const double tb = fmin(fmin(s1, s2), s3);
     ok = ok && fold_a && (tb < 2147483648.0);
     // the block sum accumulates 1.5*2^23 + T in f32 on the tensor core: exact while every partial sum
     // stays in (2^23, 2^24), i.e. |partial sums of T| < 2^22, which tb bounds
     const bool sum = ok && fold_b && (tb < 4194304.0);
-    uint8_t code = sum ? PATH_SUM : (ok ? PATH_INT : PATH_F64);
+    // mixed path: the block sum of the other groups on the tensor core as above (word 0), the separate
+    // group as an integer-path word (word 1, whose bound tmax already holds); |T| < 2^31 as above
+    // (NVFP4 only: MXFP4 blocks rarely miss the block-sum path and its epilogue keeps one path less)
+    const bool mixed = FMT == EMU_FMT_NVFP4 && ok && fold_rest && (fmin(fmin(r1, r2), r3) < 4194304.0);
+    uint8_t code = sum ? PATH_SUM : mixed ? (uint8_t)(PATH_MIXED | (gx << PATH_GROUP_SHIFT)) : (ok ? PATH_INT : PATH_F64);
     if (FMT == EMU_FMT_NVFP4) {
       code |= PATH_NORMAL;   // |acc| < 2^40 and every term a multiple of 2^-20: always in range
     } else {
@@ -566,7 +609,8 @@ static_assert(128 * REG_LOW + 32 * EPI * REG_HIGH <= 32 * NUM_WARPS * LAUNCH_REG
 template <int FMT, int RM, bool CMP>
 __global__ void __launch_bounds__(32 * NUM_WARPS, 1)
 emul_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                    const __grid_constant__ CUtensorMap tmAF, const __grid_constant__ CUtensorMap tmBF, const Params p) {
+                    const __grid_constant__ CUtensorMap tmAF, const __grid_constant__ CUtensorMap tmBF,
+                    const __grid_constant__ CUtensorMap tmBM, const Params p) {
   constexpr int NUM_EPI_WARPS = EPI;
   constexpr int CPT = BN / (EPI / 4);                         // columns per epilogue thread (16 or 32)
   constexpr int CW = CPT == 32 ? 16 : 8;                      // integer / f64 path: columns per TMEM trip
@@ -604,6 +648,7 @@ emul_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
     ptx::prefetch_tmap(&tmB);
     ptx::prefetch_tmap(&tmAF);
     ptx::prefetch_tmap(&tmBF);
+    ptx::prefetch_tmap(&tmBM);
   }
   if (warp == 1) {
     ptx::tmem_alloc(tmem_slot, 512);
@@ -640,19 +685,22 @@ emul_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
             ok = ptx::mbar_wait(&empty[s], (uint32_t)((it / NSTAGE) & 1) ^ 1u, p.err, 1);
             if (!ok) break;
             uint8_t* sa = stage_base + s * STAGE_BYTES;
-            // block-sum blocks read both folded operands, integer blocks the folded A, f64 blocks neither
+            // block-sum blocks read both folded operands, mixed blocks the folded A and the mixed B,
+            // integer blocks the folded A, f64 blocks neither
             const int path = p.path[(tm * p.tiles_n + tn) * p.nb + kb] & 3;
             ptx::mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
             ptx::tma_load_2d(sa, path != PATH_F64 ? &tmAF : &tmA, &full[s], (int)(kb * BK), (int)(tm * BM));
-            ptx::tma_load_2d(sa + A_BYTES, path == PATH_SUM ? &tmBF : &tmB, &full[s], (int)(kb * BK),
-                             (int)(tn * BN));
+            ptx::tma_load_2d(sa + A_BYTES, path == PATH_SUM ? &tmBF : path == PATH_MIXED ? &tmBM : &tmB, &full[s],
+                             (int)(kb * BK), (int)(tn * BN));
             const int q = (int)(it % NCR);
             ok = ptx::mbar_wait(&cr_empty[q], (uint32_t)((it / NCR) & 1) ^ 1u, p.err, 2);
             if (!ok) break;
             // column record bytes each path reads: block-sum the column factors, integer also the
             // multipliers and bias constants, f64 the f64 scales as well
             const uint32_t c_off = path == PATH_SUM ? (uint32_t)CR_CS : 0u;
-            const uint32_t c_len = path == PATH_SUM ? (uint32_t)(BN * 8) : path == PATH_INT ? (uint32_t)(CR_CS + BN * 8) : CR_TX;
+            const uint32_t c_len = path == PATH_SUM                          ? (uint32_t)(BN * 8)
+                                   : (path == PATH_INT || path == PATH_MIXED) ? (uint32_t)(CR_CS + BN * 8)
+                                                                              : CR_TX;
             ptx::mbar_arrive_expect_tx(&cr_full[q], c_len + RR_BYTES);
             ptx::bulk_load(cr_ring + q * CR_BYTES + c_off, p.colrec + (kb * p.tiles_n + tn) * CR_BYTES + c_off, c_len,
                            &cr_full[q]);
@@ -678,7 +726,8 @@ emul_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
           for (int64_t kb = 0; kb < p.nb && ok; ++kb, ++it) {
             const int s = (int)(it % NSTAGE);
             const int set = (int)(it % NSETS);
-            const int path = path_row[kb] & 3;
+            const int pcode = path_row[kb];
+            const int path = pcode & 3;
             ok = ptx::mbar_wait(&tm_empty[set], (uint32_t)((it / NSETS) & 1) ^ 1u, p.err, 3);
             if (!ok) break;
             ok = ptx::mbar_wait(&full[s], (uint32_t)((it / NSTAGE) & 1), p.err, 4);
@@ -695,6 +744,17 @@ emul_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
 #pragma unroll
               for (int kk = 0; kk < BK / 16; ++kk)
                 ptx::mma_f16(d_col, ptx::smem_desc_sw128(a_addr + 32 * kk), ptx::smem_desc_sw128(b_addr + 32 * kk), IDESC, 1);
+            } else if (FMT == EMU_FMT_NVFP4 && path == PATH_MIXED) {
+              // word 0: bias + every group but gx; word 1: bias + group gx (plain B values)
+              const int gx = (pcode >> PATH_GROUP_SHIFT) & 3;
+              constexpr int KPG = Fmt<FMT>::GS / 16;
+              ptx::mma_f16(d_col, bias_a, bias_b, IDESC, 0);
+              ptx::mma_f16(d_col + BN, bias_a, bias_b, IDESC, 0);
+#pragma unroll
+              for (int kk = 0; kk < BK / 16; ++kk) {
+                const uint32_t d = kk / KPG == gx ? d_col + BN : d_col;
+                ptx::mma_f16(d, ptx::smem_desc_sw128(a_addr + 32 * kk), ptx::smem_desc_sw128(b_addr + 32 * kk), IDESC, 1);
+              }
             } else {
               // one accumulator per group; integer blocks start each from the 1.5*2^23 bias
               constexpr int KPG = Fmt<FMT>::GS / 16;   // K16 steps per group
@@ -785,6 +845,38 @@ emul_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
           } else {
             sum_update16<RM, false, 0>(acc, v0, cs + col0, rs_hi, rs_c_sum);
             if constexpr (CPT == 32) sum_update16<RM, false, 16>(acc, v1, cs + col0, rs_hi, rs_c_sum);
+          }
+        } else if (FMT == EMU_FMT_NVFP4 && path == PATH_MIXED) {
+          // word 0 = 1.5*2^23 + the other groups' block sum, word 1 = 1.5*2^23 + group gx with the plain B
+          // values: T = (w0 - bias) + (w1 - bias) * sbq_gx, formed mod 2^32 as T + 2^31 like the integer path
+          const int gx = (pcode >> PATH_GROUP_SHIFT) & 3;
+          float w0[CPT / 16][16], w1[CPT / 16][16];
+#pragma unroll
+          for (int h = 0; h < CPT / 16; ++h) {
+            ptx::tmem_ld16(tmem_base + lane_base + (uint32_t)(set * SET_COLS + col0 + 16 * h), w0[h]);
+            ptx::tmem_ld16(tmem_base + lane_base + (uint32_t)(set * SET_COLS + BN + col0 + 16 * h), w1[h]);
+          }
+          ptx::tmem_wait_ld();
+          ptx::tc_fence_before();
+          __syncwarp();
+          if (lane == 0) ptx::mbar_arrive(&tm_empty[set]);
+#pragma unroll
+          for (int j4 = 0; j4 < CPT / 4; ++j4) {
+            const int cb = col0 + j4 * 4;
+            const int4 q4 = *reinterpret_cast<const int4*>(&sbq[gx * BN + cb]);
+            const double2 c01 = *reinterpret_cast<const double2*>(&cs[cb]);
+            const double2 c23 = *reinterpret_cast<const double2*>(&cs[cb + 2]);
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) {
+              const int j = j4 * 4 + jj;
+              const uint32_t q = (uint32_t)(jj == 0 ? q4.x : jj == 1 ? q4.y : jj == 2 ? q4.z : q4.w);
+              const uint32_t s32 = __float_as_uint(w0[j / 16][j % 16]) + __float_as_uint(w1[j / 16][j % 16]) * q +
+                                   (F_TO_T31 - MAGIC_BITS * q);
+              const double cv = jj == 0 ? c01.x : jj == 1 ? c01.y : jj == 2 ? c23.x : c23.y;
+              const double tf = __dadd_rn(__hiloint2double((int)rs_hi, (int)s32), -rs_c);
+              const double x = __fma_rn(tf, cv, acc[j]);
+              acc[j] = fast ? round24<RM>(x) : round_to_f32_in_f64<RM>(x);
+            }
           }
         } else
 #pragma unroll
@@ -980,7 +1072,7 @@ static bool make_map_2d(CUtensorMap* m, CUtensorMapDataType dt, void* base, uint
 static size_t align_up(size_t x) { return (x + 1023) & ~(size_t)1023; }
 
 struct WsLayout {
-  size_t a16, b16, af16, bf16, rmaq, rowrec, rw, row_nan, rinf, colrec, col_nan, cinf, ast, bst, rts, rtm, rtinf, cts, ctm, ctinf,
+  size_t a16, b16, af16, bf16, bm16, rmaq, rowrec, rw, row_nan, rinf, colrec, col_nan, cinf, ast, bst, rts, rtm, rtinf, cts, ctm, ctinf,
       path, rng_r, rng_c, err, zero_begin, zero_end, total;
 };
 
@@ -995,6 +1087,7 @@ static WsLayout layout(int fmt, int64_t M, int64_t N, int64_t K) {
   L.b16 = take((size_t)N * K * 2);
   L.af16 = take((size_t)M * K * 2);
   L.bf16 = take((size_t)N * K * 2);
+  L.bm16 = take(fmt == EMU_FMT_NVFP4 ? (size_t)N * K * 2 : 0);
   L.rmaq = take((size_t)M * G * 4);
   L.rowrec = take((size_t)nb * tiles_m * RR_BYTES);
   L.rw = take((size_t)M * G * 16);
@@ -1088,15 +1181,18 @@ static cudaError_t run_tc(const uint8_t* A, const uint8_t* B, const uint8_t* SA,
   __half* af16 = reinterpret_cast<__half*>(ws + L.af16);
   __half* bf16 = reinterpret_cast<__half*>(ws + L.bf16);
   fold_rows_kernel<<<grid_for(M * K / 8), 256, 0, stream>>>(a16, M, K, GS, T.rmaq, af16);
-  fold_cols_kernel<FMT><<<grid_for(N * K / 8), 256, 0, stream>>>(b16, N, K, tiles_n, T.colrec, bf16);
+  __half* bm16 = reinterpret_cast<__half*>(ws + L.bm16);
+  fold_cols_kernel<FMT><<<grid_for(N * K / 8), 256, 0, stream>>>(b16, N, K, tiles_n, T.colrec, T.ctm, bf16, bm16);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
 
-  CUtensorMap tmA, tmB, tmAF, tmBF;
+  CUtensorMap tmA, tmB, tmAF, tmBF, tmBM;
   if (!make_map_2d(&tmA, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a16, K, M, K * 2, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B) ||
       !make_map_2d(&tmB, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, b16, K, N, K * 2, BK, BN, CU_TENSOR_MAP_SWIZZLE_128B) ||
       !make_map_2d(&tmAF, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, af16, K, M, K * 2, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !make_map_2d(&tmBF, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, bf16, K, N, K * 2, BK, BN, CU_TENSOR_MAP_SWIZZLE_128B))
+      !make_map_2d(&tmBF, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, bf16, K, N, K * 2, BK, BN, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !make_map_2d(&tmBM, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, FMT == EMU_FMT_NVFP4 ? bm16 : bf16, K, N, K * 2, BK, BN,
+                   CU_TENSOR_MAP_SWIZZLE_128B))
     return cudaErrorInvalidValue;
 
   Params prm;
@@ -1123,7 +1219,7 @@ static cudaError_t run_tc(const uint8_t* A, const uint8_t* B, const uint8_t* SA,
   auto launch = [&](auto kern, int threads) -> cudaError_t {
     cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
     if (err != cudaSuccess) return err;
-    kern<<<grid, threads, SMEM_BYTES, stream>>>(tmA, tmB, tmAF, tmBF, prm);
+    kern<<<grid, threads, SMEM_BYTES, stream>>>(tmA, tmB, tmAF, tmBF, tmBM, prm);
     return cudaSuccess;
   };
   if (args.cmp_ref)

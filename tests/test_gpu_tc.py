@@ -110,3 +110,41 @@ def test_tc_8192_sampled_against_oracle():
     ref = oracle.emul_gemm(a[rows], b[cs], lin(sfa, rows), lin(sfb, cs), scale_fmt=0, group_size=16, w_reduce=4,
                            alpha=al, out_mode=0)
     assert nan_equal_mismatches(got[np.ix_(rows, cs)], ref, "float16") == 0
+
+
+OUTLIER_CASES = [("nvfp", True, 0, 0, 0, 100.0), ("nvfp", False, 1, 1, 1, 100.0), ("nvfp", True, 1, 0, 2, 1000.0),
+                 ("nvfp", False, 0, 1, 0, 30.0), ("mxfp", True, 0, 0, 1, 1000.0), ("mxfp", False, 1, 1, 0, 1e4)]
+
+
+@pytest.mark.parametrize("kind,absval,r3,r4,out,factor", OUTLIER_CASES,
+                         ids=[f"{k}-{'abs' if a else 'signed'}-r{r3}{r4}-o{o}-x{f:g}" for k, a, r3, r4, o, f in OUTLIER_CASES])
+def test_tc_outlier_channels(kind, absval, r3, r4, out, factor):
+    """The benchmark's input recipe at 256x192x4096: 1% of the K channels scaled in both A and B, so
+    the K blocks holding one of them carry a group whose scales dwarf the others' and leave the
+    block-sum path (mixed path: the other groups' block sum plus one separate group; integer path
+    otherwise).  Quantised on the device, compared bit for bit with the oracle and the CUDA-core kernel."""
+    from emugen_b200 import nvfp4_global_scales, quant_mxfp4, quant_nvfp4
+
+    g = torch.Generator().manual_seed(int(factor) + 7 * r3 + 3 * r4 + (11 if absval else 0))
+    M, N, K = 256, 192, 4096
+    xa, xb = torch.randn(M, K, generator=g), torch.randn(N, K, generator=g)
+    if absval:
+        xa, xb = xa.abs_(), xb.abs_()
+    cols = torch.randperm(K, generator=g)[:K // 100]
+    xa[:, cols] *= factor
+    xb[:, cols] *= factor
+    xa, xb = xa.half().cuda(), xb.half().cuda()
+    if kind == "nvfp":
+        gsa, gsb, al = nvfp4_global_scales(xa, xb)
+        (qa, sfa), (qb, sfb) = quant_nvfp4(xa, gsa), quant_nvfp4(xb, gsb)
+        alpha = float(al.item())
+    else:
+        (qa, sfa), (qb, sfb) = quant_mxfp4(xa), quant_mxfp4(xb)
+        alpha = None
+    a, b, sfa, sfb = qa.cpu().numpy(), qb.cpu().numpy(), sfa.cpu().numpy(), sfb.cpu().numpy()
+    got = _run(a, b, sfa, sfb, kind, r3, r4, alpha, out, "auto")
+    simt = _run(a, b, sfa, sfb, kind, r3, r4, alpha, out, "simt")
+    ref = oracle.emul_gemm(a, b, sfa, sfb, scale_fmt=0 if kind == "nvfp" else 1, group_size=16 if kind == "nvfp" else 32,
+                           w_reduce=4 if kind == "nvfp" else 2, r3=r3, r4=r4, alpha=alpha, out_mode=out)
+    assert _compare(simt, ref, out) == 0
+    assert _compare(got, ref, out) == 0
