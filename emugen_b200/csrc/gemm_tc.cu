@@ -46,6 +46,7 @@
 #include <stdlib.h>
 
 #include <algorithm>
+#include <type_traits>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -64,11 +65,12 @@ constexpr double TWO52 = 4503599627370496.0;
 constexpr int GROUP_M = 16;                             // tile raster: 16 M-tiles per band
 
 // Column record of one (K block, 64-column tile), GPB groups:
-//   int32  sbq[4][64]   mb * 2^(eb_g - eb)                       (integer path)
+//   int32  sbq[4][64]   mb * 2^(eb_g - eb)                       (integer / mixed path)
 //   uint32 kc[64]       2^31 - 2^23-bias * sum_g sbq   (mod 2^32)  (integer path)
-//   double cs[64]       2^eb * unit                               (integer path)
+//   double cs[64]       2^eb * unit                               (integer / mixed / block-sum path)
+//   float  csf[64]      the same in f32                           (block-sum path, f32 update)
 //   double sbw[4][64]   sb as f64                                 (f64 path)
-constexpr int CR_SBQ = 0, CR_KC = 1024, CR_CS = 1280, CR_SBW = 1792, CR_BYTES = 3840;
+constexpr int CR_SBQ = 0, CR_KC = 1024, CR_CS = 1280, CR_CSF = 1792, CR_SBW = 2048, CR_BYTES = 4096;
 // Row record of one (K block, 128-row tile):
 //   double2 rs[128]      row base {exponent word of 2^(52+e) (high half), (2^52 + 2^31) * 2^e}
 constexpr int RR_RS = 0, RR_BYTES = 2048;
@@ -161,6 +163,13 @@ struct PrepTables {
   uint8_t* path;        // [tiles_m][tiles_n][nb]  path code
   uint32_t* rng_r;      // [tiles_m][2]  MXFP4: max scale byte, 255 - min scale byte (zeroed per call)
   uint32_t* rng_c;      // [tiles_n][2]
+  uint32_t* rbmax;      // [tiles_m][nb] NVFP4: 512 + max row base exponent over the tile (zeroed per call)
+  uint32_t* cbmax;      // [tiles_n][nb]
+  uint32_t* rbmin;      // [tiles_m]     NVFP4: 512 - min row base exponent over the tile and all blocks
+  uint32_t* cbmin;      // [tiles_n]
+  float* tile_bound;    // [tiles_m][tiles_n] NVFP4: bound on sum_b max |s_b| (zeroed per call)
+  uint32_t* tile_other; // [tiles_m][tiles_n] blocks off the block-sum path (zeroed per call)
+  uint8_t* tile_f32;    // [tiles_m][tiles_n] 1: f32 block-sum updates are exact under RZ
 };
 
 // E4M3 -> (signed significand, exponent) with value = ma * 2^sx; NaN -> ma 0.
@@ -175,6 +184,17 @@ __device__ __forceinline__ void e4m3_split(uint32_t byte, int& ma, int& sx, bool
 
 __device__ __forceinline__ double pow2d(int e) {   // exact 2^e for e in [-1022, 1023]
   return __longlong_as_double((long long)(e + 1023) << 52);
+}
+
+__device__ __forceinline__ float pow2f(int e) {    // exact 2^e for e in [-149, 127]
+  return e >= -126 ? __int_as_float((e + 127) << 23) : __int_as_float(1 << (e + 149));
+}
+
+// atomicMax of v over the active lanes of a warp whose lanes share `slot`
+__device__ __forceinline__ void warp_atomic_max(uint32_t* slot, uint32_t v) {
+  const unsigned mask = __activemask();
+  v = __reduce_max_sync(mask, v);
+  if ((threadIdx.x & 31) == __ffs(mask) - 1) atomicMax(slot, v);
 }
 
 // Row base record for exponent e: x = double{hi = exponent word of 2^(52+e), lo = T + 2^31} is
@@ -239,6 +259,8 @@ __global__ void row_tables_kernel(const uint8_t* __restrict__ sf, int64_t M, int
       }
       *rs = row_base(base - 1);     // v = p4*ma*mb*2^(sxa+sxb-2)
       if (any_nan) atomicOr(&t.row_nan[r], 1u);
+      warp_atomic_max(&t.rbmax[(r / BM) * nb + kb], (uint32_t)(base + 512));
+      warp_atomic_max(&t.rbmin[r / BM], (uint32_t)(512 - base));
     } else {
       int base = 1 << 30;
       bool inf = false;
@@ -275,6 +297,7 @@ __global__ void col_tables_kernel(const uint8_t* __restrict__ sf, int64_t N, int
     int32_t* sbq = reinterpret_cast<int32_t*>(rec + CR_SBQ);
     uint32_t* kc = reinterpret_cast<uint32_t*>(rec + CR_KC);
     double* cs = reinterpret_cast<double*>(rec + CR_CS);
+    float* csf = reinterpret_cast<float*>(rec + CR_CSF);
     double* sbw = reinterpret_cast<double*>(rec + CR_SBW);
     uint32_t sum = 0;
     if (n >= N) {
@@ -282,6 +305,7 @@ __global__ void col_tables_kernel(const uint8_t* __restrict__ sf, int64_t N, int
       for (int g = 0; g < GPB; ++g) { sbq[g * BN + c] = 0; sbw[g * BN + c] = 0.0; }
       kc[c] = 0x80000000u;
       cs[c] = 0.0;
+      csf[c] = 0.0f;
       t.cinf[n * nb + kb] = 0;
       continue;
     }
@@ -307,7 +331,10 @@ __global__ void col_tables_kernel(const uint8_t* __restrict__ sf, int64_t N, int
         sbw[g * BN + c] = (double)mb[g] * pow2d(sx[g]);
       }
       cs[c] = pow2d(base - 1);
+      csf[c] = pow2f(base - 1);
       if (any_nan) atomicOr(&t.col_nan[n], 1u);
+      warp_atomic_max(&t.cbmax[tn * nb + kb], (uint32_t)(base + 512));
+      warp_atomic_max(&t.cbmin[tn], (uint32_t)(512 - base));
       t.cinf[n * nb + kb] = 0;
     } else {
       int base = 1 << 30;
@@ -328,6 +355,7 @@ __global__ void col_tables_kernel(const uint8_t* __restrict__ sf, int64_t N, int
         sbw[g * BN + c] = ue8m0_quarter_f64(byte[g]) * 4.0;
       }
       cs[c] = pow2d(base - 128);
+      csf[c] = pow2f(base - 128);
       t.cinf[n * nb + kb] = inf ? 1 : 0;
       scale_range(byte, GPB, t.rng_c + 2 * tn);
     }
@@ -506,6 +534,10 @@ __global__ void decide_kernel(int64_t tiles_m, int64_t tiles_n, int64_t nb, int6
     uint8_t code = sum ? PATH_SUM : mixed ? (uint8_t)(PATH_MIXED | (gx << PATH_GROUP_SHIFT)) : (ok ? PATH_INT : PATH_F64);
     if (FMT == EMU_FMT_NVFP4) {
       code |= PATH_NORMAL;   // |acc| < 2^40 and every term a multiple of 2^-20: always in range
+      // |s_b| <= tb * 2^(row base + column base - 2) for every output of the tile pair
+      const int eb = (int)t.rbmax[tm * nb + kb] + (int)t.cbmax[tn * nb + kb] - 1024 - 2;
+      const float sabs = ok ? (float)(tb * margin * pow2d(eb)) : __int_as_float(0x7F800000);
+      atomicAdd(&t.tile_bound[tm * tiles_n + tn], sabs);
     } else {
       // every block term is a multiple of 2^(minA + minB - 256) and at most 9216 * 2^(maxA + maxB - 256):
       // no accumulator value is subnormal or reaches 2^127 when these hold for the whole tile pair
@@ -515,6 +547,37 @@ __global__ void decide_kernel(int64_t tiles_m, int64_t tiles_n, int64_t nb, int6
         code |= PATH_NORMAL;
     }
     t.path[i] = code;
+    if ((code & 3) != PATH_SUM) atomicAdd(&t.tile_other[tm * tiles_n + tn], 1u);
+  }
+}
+
+// Per tile pair: may the block-sum path update the accumulator in f32 under RZ rounding?  The f32
+// update computes RZ32(acc + s) in one FMA; the reference computes RZ32(RN64(acc + s)).  They agree
+// whenever acc + s is exact in f64, i.e. below 2^53 quanta.  NVFP4: every term of the tile pair is a
+// multiple of 2^(min row base + min column base - 2), so is the accumulator (rounding a multiple of a
+// power of two to f32 keeps it one), and |acc + s| <= sum_b max |s_b| (RZ never grows a magnitude
+// while every sum is exact), bounded by the decide kernel's per-block bounds (2^-16 of margin for
+// their f32 summation).  MXFP4: the terms are multiples of 2^(minA + minB - 256), the accumulator
+// below nb * 9216 * 2^(maxA + maxB - 256).
+// (RNE needs no bound: with both addends 24-bit numbers, rounding to f64 first never changes the
+// f32 result.)  Tile pairs where more than a quarter of the blocks leave the block-sum path stay in
+// f64 throughout: every switch of representation costs about as much as the f32 update saves.
+template <int FMT>
+__global__ void tile_f32_kernel(int64_t tiles_m, int64_t tiles_n, int64_t nb, int rm, PrepTables t) {
+  int lg_nb = 0;
+  while ((1ll << lg_nb) < nb) ++lg_nb;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < tiles_m * tiles_n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t tm = i / tiles_n, tn = i % tiles_n;
+    bool ok;
+    if (FMT == EMU_FMT_NVFP4) {
+      const int qe = (512 - (int)t.rbmin[tm]) + (512 - (int)t.cbmin[tn]) - 2;
+      ok = (double)t.tile_bound[i] < (1.0 - 0x1p-16) * pow2d(53 + qe);
+    } else {
+      const int maxa = (int)t.rng_r[2 * tm], mina = 255 - (int)t.rng_r[2 * tm + 1];
+      const int maxb = (int)t.rng_c[2 * tn], minb = 255 - (int)t.rng_c[2 * tn + 1];
+      ok = maxa < 255 && maxb < 255 && (maxa + maxb) - (mina + minb) + 14 + lg_nb <= 52;
+    }
+    t.tile_f32[i] = ((rm == EMU_RNE || ok) && 4 * (int64_t)t.tile_other[i] <= nb) ? 1 : 0;
   }
 }
 
@@ -531,6 +594,7 @@ struct Params {
   const uint32_t* col_nan;
   const uint8_t* colrec;
   const uint8_t* path;
+  const uint8_t* tile_f32;
   const float* alpha;
   void* out;
   int* err;
@@ -593,6 +657,34 @@ __device__ __forceinline__ void sum_update16(double (&acc)[CPT], const float (&v
   }
 }
 
+// f32 form of the block-sum update, the accumulator's f32 value kept in the low half of acc[]:
+// s = T * 2^e_row * 2^e_col with T = word - 1.5*2^23 (|T| < 2^22), acc = R4(acc + s) in one FMA.
+// NVFP4: T * 2^e_row = word * 2^e_row - 1.5*2^23 * 2^e_row exactly (e_row >= -10); MXFP4: 2^e_row *
+// 2^e_col is exact (a normal product when the tile pair passes the range test).
+template <int FMT, int RM, int OFF, int CPT>
+__device__ __forceinline__ void sum_update16_f32(double (&acc)[CPT], const float (&v)[16], const float* csf, float cr) {
+  const float ncr = -MAGIC_F * cr;
+#pragma unroll
+  for (int j = 0; j < 16; j += 4) {
+    const float4 c4 = *reinterpret_cast<const float4*>(&csf[OFF + j]);
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+      const float c = h == 0 ? c4.x : h == 1 ? c4.y : h == 2 ? c4.z : c4.w;
+      const float a = __int_as_float(__double2loint(acc[OFF + j + h]));
+      float r;
+      if (FMT == EMU_FMT_NVFP4) {
+        const float t = __fmaf_rn(v[j + h], cr, ncr);
+        r = RM == EMU_RZ ? __fmaf_rz(t, c, a) : __fmaf_rn(t, c, a);
+      } else {
+        const float t = __fadd_rn(v[j + h], -MAGIC_F);
+        const float crc = __fmul_rn(cr, c);
+        r = RM == EMU_RZ ? __fmaf_rz(t, crc, a) : __fmaf_rn(t, crc, a);
+      }
+      acc[OFF + j + h] = __hiloint2double(__double2hiint(acc[OFF + j + h]), __float_as_int(r));
+    }
+  }
+}
+
 // Warpgroup 0 = producer (warp 0), MMA issuer and TMEM owner (warp 1), two idle warps; then EPI
 // epilogue warps, each thread owning one row and CPT = 64 / (EPI / 4) columns of the 64-column tile.
 // Registers move from warpgroup 0 to the epilogue (setmaxnreg); the split never exceeds what the CTA
@@ -615,6 +707,9 @@ emul_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
   constexpr int CPT = BN / (EPI / 4);                         // columns per epilogue thread (16 or 32)
   constexpr int CW = CPT == 32 ? 16 : 8;                      // integer / f64 path: columns per TMEM trip
   constexpr int GPB = Fmt<FMT>::GPB;
+  // f32 block-sum updates compiled in (MXFP4, and NVFP4 under RNE; for NVFP4 under RZ the extra
+  // code costs the f64 paths more in register spills than the f32 update saves on the benchmark mix)
+  constexpr bool F32 = FMT == EMU_FMT_MXFP4 || RM == EMU_RNE;
   constexpr int SET_COLS = GPB * BN;                         // TMEM columns per K block
   constexpr int NSETS = 512 / SET_COLS;                      // 2 (NVFP4) or 4 (MXFP4)
   constexpr uint32_t CR_TX = (FMT == EMU_FMT_NVFP4) ? CR_BYTES : (uint32_t)(CR_SBW + 2 * BN * 8);
@@ -698,7 +793,7 @@ emul_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
             // column record bytes each path reads: block-sum the column factors, integer also the
             // multipliers and bias constants, f64 the f64 scales as well
             const uint32_t c_off = path == PATH_SUM ? (uint32_t)CR_CS : 0u;
-            const uint32_t c_len = path == PATH_SUM                          ? (uint32_t)(BN * 8)
+            const uint32_t c_len = path == PATH_SUM                          ? (uint32_t)(BN * 12)
                                    : (path == PATH_INT || path == PATH_MIXED) ? (uint32_t)(CR_CS + BN * 8)
                                                                               : CR_TX;
             ptx::mbar_arrive_expect_tx(&cr_full[q], c_len + RR_BYTES);
@@ -798,10 +893,12 @@ emul_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
       double acc[CPT];
 #pragma unroll
       for (int j = 0; j < CPT; ++j) acc[j] = 0.0;
-
+      // f32 block-sum updates (exact under RNE always, under RZ when the tile pair's bound allows)
+      const bool tile32 = p.tile_f32[tm * p.tiles_n + tn] != 0;
+      bool in32 = false;                       // acc[] holds f32 values in its low halves
       const uint8_t* path_row = p.path + (tm * p.tiles_n + tn) * p.nb;
-      int nx_path = path_row[0];
       const int rl = quarter * 32 + lane;      // row within the tile
+      int nx_path = path_row[0];
       for (int64_t kb = 0; kb < p.nb && ok; ++kb, ++it) {
         const int set = (int)(it % NSETS);
         const int q = (int)(it % NCR);
@@ -825,8 +922,29 @@ emul_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
         const double2 rsv = reinterpret_cast<const double2*>(rr + RR_RS)[rl];
         const uint32_t rs_hi = (uint32_t)__double2hiint(rsv.x);
         const double rs_c = rsv.y;
+        const bool use32 = F32 && tile32 && path == PATH_SUM && fast;
+        if (use32 != in32) {
+          // switch the accumulator's representation (exact both ways: acc holds f32 values)
+#pragma unroll
+          for (int j = 0; j < CPT; ++j)
+            acc[j] = use32 ? __hiloint2double(0, __float_as_int(__double2float_rn(acc[j])))
+                           : (double)__int_as_float(__double2loint(acc[j]));
+          in32 = use32;
+        }
 
-        if (path == PATH_SUM) {
+        if (use32) {
+          float v0[16], v1[16];
+          ptx::tmem_ld16(tmem_base + lane_base + (uint32_t)(set * SET_COLS + col0), v0);
+          if constexpr (CPT == 32) ptx::tmem_ld16(tmem_base + lane_base + (uint32_t)(set * SET_COLS + col0 + 16), v1);
+          ptx::tmem_wait_ld();
+          ptx::tc_fence_before();
+          __syncwarp();
+          if (lane == 0) ptx::mbar_arrive(&tm_empty[set]);
+          const float* csf = reinterpret_cast<const float*>(cr + CR_CSF) + col0;
+          const float crf = pow2f((int)(rs_hi >> 20) - 1075);
+          sum_update16_f32<FMT, RM, 0>(acc, v0, csf, crf);
+          if constexpr (CPT == 32) sum_update16_f32<FMT, RM, 16>(acc, v1, csf, crf);
+        } else if (path == PATH_SUM) {
           // the row constant for words 0x4B400000 + T instead of T + 2^31 (exact: multiples of 2^e)
           const double rs_c_sum = __fma_rn(-(double)F_TO_T31 * 0x1p-52, __hiloint2double((int)rs_hi, 0), rs_c);
           // block-sum path: one TMEM word per output; all CPT are loaded before a single wait, so the
@@ -976,6 +1094,10 @@ emul_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
         if (lane == 0) ptx::mbar_arrive(&cr_empty[q]);
       }
       if (!ok) break;
+      if (in32) {
+#pragma unroll
+        for (int j = 0; j < CPT; ++j) acc[j] = (double)__int_as_float(__double2loint(acc[j]));
+      }
       // ---- output (and the optional fused comparison with a reference output, emu_compare's rules)
       unsigned long long c_cnt = 0;
       long long c_first = 0x7FFFFFFFFFFFFFFFll;
@@ -1073,7 +1195,7 @@ static size_t align_up(size_t x) { return (x + 1023) & ~(size_t)1023; }
 
 struct WsLayout {
   size_t a16, b16, af16, bf16, bm16, rmaq, rowrec, rw, row_nan, rinf, colrec, col_nan, cinf, ast, bst, rts, rtm, rtinf, cts, ctm, ctinf,
-      path, rng_r, rng_c, err, zero_begin, zero_end, total;
+      path, tile_f32, rng_r, rng_c, rbmax, cbmax, tile_bound, tile_other, rbmin, cbmin, err, zero_begin, zero_end, total;
 };
 
 static WsLayout layout(int fmt, int64_t M, int64_t N, int64_t K) {
@@ -1103,11 +1225,18 @@ static WsLayout layout(int fmt, int64_t M, int64_t N, int64_t K) {
   L.ctm = take((size_t)tiles_n * G * 16);
   L.ctinf = take((size_t)tiles_n * nb);
   L.path = take((size_t)tiles_m * tiles_n * nb);
+  L.tile_f32 = take((size_t)tiles_m * tiles_n);
   L.zero_begin = off;                       // regions cleared before every call
   L.row_nan = take((size_t)M * 4);
   L.col_nan = take((size_t)Np * 4);
   L.rng_r = take((size_t)tiles_m * 8);
   L.rng_c = take((size_t)tiles_n * 8);
+  L.rbmax = take((size_t)tiles_m * nb * 4);
+  L.cbmax = take((size_t)tiles_n * nb * 4);
+  L.tile_bound = take((size_t)tiles_m * tiles_n * 4);
+  L.tile_other = take((size_t)tiles_m * tiles_n * 4);
+  L.rbmin = take((size_t)tiles_m * 4);
+  L.cbmin = take((size_t)tiles_n * 4);
   L.err = take(16);
   L.zero_end = off;
   L.total = off;
@@ -1161,6 +1290,13 @@ static cudaError_t run_tc(const uint8_t* A, const uint8_t* B, const uint8_t* SA,
   T.path = ws + L.path;
   T.rng_r = reinterpret_cast<uint32_t*>(ws + L.rng_r);
   T.rng_c = reinterpret_cast<uint32_t*>(ws + L.rng_c);
+  T.rbmax = reinterpret_cast<uint32_t*>(ws + L.rbmax);
+  T.cbmax = reinterpret_cast<uint32_t*>(ws + L.cbmax);
+  T.tile_bound = reinterpret_cast<float*>(ws + L.tile_bound);
+  T.tile_other = reinterpret_cast<uint32_t*>(ws + L.tile_other);
+  T.rbmin = reinterpret_cast<uint32_t*>(ws + L.rbmin);
+  T.cbmin = reinterpret_cast<uint32_t*>(ws + L.cbmin);
+  T.tile_f32 = ws + L.tile_f32;
 
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
@@ -1178,6 +1314,8 @@ static cudaError_t run_tc(const uint8_t* A, const uint8_t* B, const uint8_t* SA,
   tile_stats_kernel<FMT><<<grid_for(tiles_m * G), 256, 0, stream>>>(M, BM, tiles_m, G, nb, 0, T);
   tile_stats_kernel<FMT><<<grid_for(tiles_n * G), 256, 0, stream>>>(N, BN, tiles_n, G, nb, 1, T);
   decide_kernel<FMT><<<grid_for(tiles_m * tiles_n * nb), 256, 0, stream>>>(tiles_m, tiles_n, nb, G, T);
+  tile_f32_kernel<FMT><<<grid_for(tiles_m * tiles_n), 256, 0, stream>>>(
+      tiles_m, tiles_n, nb, nb == 1 ? args.stage3_rounding : args.stage4_rounding, T);
   __half* af16 = reinterpret_cast<__half*>(ws + L.af16);
   __half* bf16 = reinterpret_cast<__half*>(ws + L.bf16);
   fold_rows_kernel<<<grid_for(M * K / 8), 256, 0, stream>>>(a16, M, K, GS, T.rmaq, af16);
@@ -1204,6 +1342,7 @@ static cudaError_t run_tc(const uint8_t* A, const uint8_t* B, const uint8_t* SA,
   prm.col_nan = T.col_nan;
   prm.colrec = T.colrec;
   prm.path = T.path;
+  prm.tile_f32 = T.tile_f32;
   prm.alpha = alpha;
   prm.out = out;
   prm.err = reinterpret_cast<int*>(ws + L.err);
