@@ -83,8 +83,10 @@ constexpr int PATH_GROUP_SHIFT = 3;
 // the 128-byte-swizzled K-major layout, so one K=16 MMA writes 3072 * 4096 = 1.5 * 2^23 everywhere.
 constexpr int BIAS_BYTES = A_BYTES + B_BYTES;
 // mbarriers (full/empty per stage, cr_full/cr_empty per record slot, 4 + 4 TMEM-set barriers, drain)
-// and the TMEM address word, after the rings; the leading 1024 bytes cover aligning the base to 1024
-constexpr int BAR_BYTES = (2 * NSTAGE + 2 * NCR + 9) * 8 + 8;
+// the TMEM address word and one path byte per stage, after the rings; the leading 1024 bytes cover
+// aligning the base to 1024
+constexpr int BAR_BYTES = (2 * NSTAGE + 2 * NCR + 9) * 8 + 8 + 8;
+static_assert(NSTAGE <= 8, "one path byte per stage after the TMEM address word");
 constexpr int SMEM_BYTES = 1024 + NSTAGE * STAGE_BYTES + BIAS_BYTES + NCR * (CR_BYTES + RR_BYTES) + BAR_BYTES;
 static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
 constexpr uint32_t F_TO_T31 = 0x80000000u - MAGIC_BITS;   // (T + 0x4B400000) + this = T + 2^31 (mod 2^32)
@@ -169,7 +171,7 @@ struct PrepTables {
   uint32_t* cbmin;      // [tiles_n]
   float* tile_bound;    // [tiles_m][tiles_n] NVFP4: bound on sum_b max |s_b| (zeroed per call)
   uint32_t* tile_other; // [tiles_m][tiles_n] blocks off the block-sum path (zeroed per call)
-  uint8_t* tile_f32;    // [tiles_m][tiles_n] 1: f32 block-sum updates are exact under RZ
+  uint8_t* tile_f32;    // [tiles_m][tiles_n] 1: the tile pair goes to the launch with f32 block-sum updates
 };
 
 // E4M3 -> (signed significand, exponent) with value = ma * 2^sx; NaN -> ma 0.
@@ -594,22 +596,71 @@ struct Params {
   const uint32_t* col_nan;
   const uint8_t* colrec;
   const uint8_t* path;
-  const uint8_t* tile_f32;
+  const uint32_t* tile_list;     // tile pairs (tm << 16 | tn) this launch processes, raster order
+  const uint32_t* tile_count;    // their number (device memory)
   const float* alpha;
   void* out;
   int* err;
   int r3, r4, out_mode;
 };
 
-__device__ __forceinline__ void tile_coords(int64_t t, const Params& p, int64_t& tm, int64_t& tn) {
-  const int64_t per_band = (int64_t)GROUP_M * p.tiles_n;
+__device__ __forceinline__ void tile_coords(int64_t t, int64_t tiles_m, int64_t tiles_n, int64_t& tm, int64_t& tn) {
+  const int64_t per_band = (int64_t)GROUP_M * tiles_n;
   const int64_t band = t / per_band;
   const int64_t first_m = band * GROUP_M;
-  const int64_t rem = p.tiles_m - first_m;
+  const int64_t rem = tiles_m - first_m;
   const int64_t gm = rem < GROUP_M ? rem : (int64_t)GROUP_M;
   const int64_t idx = t % per_band;
   tm = first_m + idx % gm;
   tn = idx / gm;
+}
+
+// Splits the tile pairs, in raster order (bands of GROUP_M row tiles), into the list of the launch
+// without f32 updates (counts[0] of them) and the list of the f32 launch (counts[1]), by the tile flag.
+// One CTA of 1024 threads, a block-wide scan per chunk of 1024 tile pairs.  Entries are tm << 16 | tn,
+// so the producer and MMA warps, which run with few registers, decode them with a shift and a mask.
+__global__ void __launch_bounds__(1024) tile_lists_kernel(int64_t tiles_m, int64_t tiles_n,
+                                                           const uint8_t* __restrict__ flag, uint32_t* __restrict__ list64,
+                                                           uint32_t* __restrict__ list32, uint32_t* __restrict__ counts) {
+  __shared__ uint32_t warp_sums[32];
+  const int64_t total = tiles_m * tiles_n;
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  int64_t done32 = 0;                      // tile pairs placed in list32 by earlier chunks
+  for (int64_t c0 = 0; c0 < total; c0 += 1024) {
+    const int64_t t = c0 + threadIdx.x;
+    uint32_t id = 0;
+    bool f = false;
+    if (t < total) {
+      int64_t tm, tn;
+      tile_coords(t, tiles_m, tiles_n, tm, tn);
+      id = (uint32_t)(tm << 16 | tn);
+      f = flag[tm * tiles_n + tn] != 0;
+    }
+    const unsigned ballot = __ballot_sync(0xFFFFFFFFu, f);
+    if (lane == 0) warp_sums[w] = __popc(ballot);
+    __syncthreads();
+    if (w == 0) {
+      uint32_t v = warp_sums[lane];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t n = __shfl_up_sync(0xFFFFFFFFu, v, o);
+        if (lane >= o) v += n;
+      }
+      warp_sums[lane] = v;                   // inclusive prefix over warps
+    }
+    __syncthreads();
+    const int64_t before = (w ? warp_sums[w - 1] : 0) + __popc(ballot & ((1u << lane) - 1));   // flagged, this chunk
+    if (t < total) {
+      if (f) list32[done32 + before] = id;
+      else list64[(c0 - done32) + (threadIdx.x - before)] = id;
+    }
+    done32 += warp_sums[31];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    counts[0] = (uint32_t)(total - done32);
+    counts[1] = (uint32_t)done32;
+  }
 }
 
 // p4 -> nearest fp16-grid value of p = p4/4, times 4
@@ -698,18 +749,18 @@ constexpr int REG_HIGH = ((32 * NUM_WARPS * LAUNCH_REGS - 128 * REG_LOW) / (32 *
 static_assert(128 * REG_LOW + 32 * EPI * REG_HIGH <= 32 * NUM_WARPS * LAUNCH_REGS, "register split exceeds the launch");
 // CMP: the comparison with a reference output is compiled in (a separate instantiation, so the plain
 // GEMM's register allocation is not affected by it).
-template <int FMT, int RM, bool CMP>
+// F32: the launch for the tile pairs whose block-sum updates run in f32 (see tile_f32_kernel); the
+// other tile pairs go to the launch without that code, whose register allocation it would disturb.
+template <int FMT, int RM, bool CMP, bool F32>
 __global__ void __launch_bounds__(32 * NUM_WARPS, 1)
 emul_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ CUtensorMap tmAF, const __grid_constant__ CUtensorMap tmBF,
                     const __grid_constant__ CUtensorMap tmBM, const Params p) {
   constexpr int NUM_EPI_WARPS = EPI;
   constexpr int CPT = BN / (EPI / 4);                         // columns per epilogue thread (16 or 32)
-  constexpr int CW = CPT == 32 ? 16 : 8;                      // integer / f64 path: columns per TMEM trip
+  // integer / f64 path: columns per TMEM trip (NVFP4: 8, its four words per column keep 32 registers)
+  constexpr int CW = FMT == EMU_FMT_NVFP4 ? 8 : (CPT == 32 ? 16 : 8);
   constexpr int GPB = Fmt<FMT>::GPB;
-  // f32 block-sum updates compiled in (MXFP4, and NVFP4 under RNE; for NVFP4 under RZ the extra
-  // code costs the f64 paths more in register spills than the f32 update saves on the benchmark mix)
-  constexpr bool F32 = FMT == EMU_FMT_MXFP4 || RM == EMU_RNE;
   constexpr int SET_COLS = GPB * BN;                         // TMEM columns per K block
   constexpr int NSETS = 512 / SET_COLS;                      // 2 (NVFP4) or 4 (MXFP4)
   constexpr uint32_t CR_TX = (FMT == EMU_FMT_NVFP4) ? CR_BYTES : (uint32_t)(CR_SBW + 2 * BN * 8);
@@ -729,9 +780,9 @@ emul_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
   uint64_t* tm_empty = tm_full + 4;            // [NSETS]
   uint64_t* drain = tm_empty + 4;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint8_t* stage_path = reinterpret_cast<uint8_t*>(drain + 2);   // [NSTAGE] path code of the block in each stage
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t total_tiles = p.tiles_m * p.tiles_n;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < NSTAGE; ++i) { ptx::mbar_init(&full[i], 1); ptx::mbar_init(&empty[i], 1); }
@@ -763,10 +814,13 @@ emul_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
   ptx::tc_fence_before();
   __syncthreads();
   ptx::tc_fence_after();
-  const uint32_t tmem_base = *tmem_slot;
   // the register limits hold for the code each call dominates, so they sit inside the role branches
   if (warp < 4) {
     ptx::setmaxnreg_dec<REG_LOW>();
+    // loaded after the register split: a loaded value held across setmaxnreg.dec may sit in a register
+    // above the new limit and be lost
+    const int64_t total_tiles = (int64_t)*p.tile_count < p.tiles_m * p.tiles_n ? (int64_t)*p.tile_count : p.tiles_m * p.tiles_n;
+    const uint32_t tmem_base = *tmem_slot;
     if (warp == 0) {
       // ---------------------------------------------------------------- producer
       if (lane == 0) {
@@ -774,7 +828,9 @@ emul_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
         bool ok = true;
         for (int64_t t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
           int64_t tm, tn;
-          tile_coords(t, p, tm, tn);
+          const uint32_t tid = p.tile_list[t];
+          tm = tid >> 16;
+          tn = tid & 0xFFFFu;
           for (int64_t kb = 0; kb < p.nb && ok; ++kb, ++it) {
             const int s = (int)(it % NSTAGE);
             ok = ptx::mbar_wait(&empty[s], (uint32_t)((it / NSTAGE) & 1) ^ 1u, p.err, 1);
@@ -782,7 +838,11 @@ emul_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
             uint8_t* sa = stage_base + s * STAGE_BYTES;
             // block-sum blocks read both folded operands, mixed blocks the folded A and the mixed B,
             // integer blocks the folded A, f64 blocks neither
-            const int path = p.path[(tm * p.tiles_n + tn) * p.nb + kb] & 3;
+            const int pcode = p.path[(tm * p.tiles_n + tn) * p.nb + kb];
+            const int path = pcode & 3;
+            // the MMA warp reads the block's path code here after its wait on full[s] (the arrive
+            // below releases this store)
+            stage_path[s] = (uint8_t)pcode;
             ptx::mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
             ptx::tma_load_2d(sa, path != PATH_F64 ? &tmAF : &tmA, &full[s], (int)(kb * BK), (int)(tm * BM));
             ptx::tma_load_2d(sa + A_BYTES, path == PATH_SUM ? &tmBF : path == PATH_MIXED ? &tmBM : &tmB, &full[s],
@@ -814,20 +874,18 @@ emul_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
         constexpr uint32_t IDESC = ptx::idesc_f16_f32(BM, BN);
         int64_t it = 0;
         bool ok = true;
+        // the same blocks as the producer, in the same order; each block's path code comes with its stage
         for (int64_t t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
-          int64_t tm, tn;
-          tile_coords(t, p, tm, tn);
-          const uint8_t* path_row = p.path + (tm * p.tiles_n + tn) * p.nb;
           for (int64_t kb = 0; kb < p.nb && ok; ++kb, ++it) {
             const int s = (int)(it % NSTAGE);
             const int set = (int)(it % NSETS);
-            const int pcode = path_row[kb];
-            const int path = pcode & 3;
             ok = ptx::mbar_wait(&tm_empty[set], (uint32_t)((it / NSETS) & 1) ^ 1u, p.err, 3);
             if (!ok) break;
             ok = ptx::mbar_wait(&full[s], (uint32_t)((it / NSTAGE) & 1), p.err, 4);
             if (!ok) break;
             ptx::tc_fence_after();
+            const int pcode = stage_path[s];
+            const int path = pcode & 3;
             const uint32_t a_addr = ptx::smem_u32(stage_base + s * STAGE_BYTES);
             const uint32_t b_addr = a_addr + A_BYTES;
             const uint32_t d_col = tmem_base + (uint32_t)(set * SET_COLS);
@@ -877,6 +935,8 @@ emul_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
     }
   } else {
     ptx::setmaxnreg_inc<REG_HIGH>();
+    const int64_t total_tiles = (int64_t)*p.tile_count < p.tiles_m * p.tiles_n ? (int64_t)*p.tile_count : p.tiles_m * p.tiles_n;
+    const uint32_t tmem_base = *tmem_slot;
     // ---------------------------------------------------------------- epilogue (warps 4..11)
     const int ew = warp - 4;                 // 0..7
     const int quarter = warp & 3;            // TMEM lane quarter this warp may access
@@ -886,15 +946,15 @@ emul_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
     bool ok = true;
     for (int64_t t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
       int64_t tm, tn;
-      tile_coords(t, p, tm, tn);
+      const uint32_t tid = p.tile_list[t];
+      tm = tid >> 16;
+      tn = tid & 0xFFFFu;
       const int64_t m = tm * BM + quarter * 32 + lane;
       const bool row_ok = m < p.M;
       const int64_t mr = row_ok ? m : (p.M - 1);
       double acc[CPT];
 #pragma unroll
       for (int j = 0; j < CPT; ++j) acc[j] = 0.0;
-      // f32 block-sum updates (exact under RNE always, under RZ when the tile pair's bound allows)
-      const bool tile32 = p.tile_f32[tm * p.tiles_n + tn] != 0;
       bool in32 = false;                       // acc[] holds f32 values in its low halves
       const uint8_t* path_row = p.path + (tm * p.tiles_n + tn) * p.nb;
       const int rl = quarter * 32 + lane;      // row within the tile
@@ -918,11 +978,10 @@ emul_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
         const uint32_t* kc = reinterpret_cast<const uint32_t*>(cr + CR_KC);
         const double* cs = reinterpret_cast<const double*>(cr + CR_CS);
         const double* sbw = reinterpret_cast<const double*>(cr + CR_SBW);
-        const uint8_t* rr = rr_ring + q * RR_BYTES;
-        const double2 rsv = reinterpret_cast<const double2*>(rr + RR_RS)[rl];
+        const double2 rsv = reinterpret_cast<const double2*>(rr_ring + q * RR_BYTES + RR_RS)[rl];
         const uint32_t rs_hi = (uint32_t)__double2hiint(rsv.x);
         const double rs_c = rsv.y;
-        const bool use32 = F32 && tile32 && path == PATH_SUM && fast;
+        const bool use32 = F32 && path == PATH_SUM && fast;
         if (use32 != in32) {
           // switch the accumulator's representation (exact both ways: acc holds f32 values)
 #pragma unroll
@@ -1158,7 +1217,7 @@ emul_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
   __syncthreads();
   if (warp == 1) {
     ptx::tc_fence_after();
-    ptx::tmem_dealloc(tmem_base, 512);
+    ptx::tmem_dealloc(*tmem_slot, 512);
   }
 }
 
@@ -1195,7 +1254,7 @@ static size_t align_up(size_t x) { return (x + 1023) & ~(size_t)1023; }
 
 struct WsLayout {
   size_t a16, b16, af16, bf16, bm16, rmaq, rowrec, rw, row_nan, rinf, colrec, col_nan, cinf, ast, bst, rts, rtm, rtinf, cts, ctm, ctinf,
-      path, tile_f32, rng_r, rng_c, rbmax, cbmax, tile_bound, tile_other, rbmin, cbmin, err, zero_begin, zero_end, total;
+      path, tile_f32, tile_list, tile_count, rng_r, rng_c, rbmax, cbmax, tile_bound, tile_other, rbmin, cbmin, err, zero_begin, zero_end, total;
 };
 
 static WsLayout layout(int fmt, int64_t M, int64_t N, int64_t K) {
@@ -1226,6 +1285,8 @@ static WsLayout layout(int fmt, int64_t M, int64_t N, int64_t K) {
   L.ctinf = take((size_t)tiles_n * nb);
   L.path = take((size_t)tiles_m * tiles_n * nb);
   L.tile_f32 = take((size_t)tiles_m * tiles_n);
+  L.tile_list = take((size_t)tiles_m * tiles_n * 8);
+  L.tile_count = take(8);
   L.zero_begin = off;                       // regions cleared before every call
   L.row_nan = take((size_t)M * 4);
   L.col_nan = take((size_t)Np * 4);
@@ -1254,6 +1315,7 @@ bool gemm_tc_supported(int fmt, int w_reduce, int64_t M, int64_t N, int64_t K) {
   if (fmt == EMU_FMT_MXFP4 && w_reduce != 2) return false;
   if (K % 64 != 0 || M < BM || N < BN) return false;   // every TMA box lies within its tensor
   if (K > (int64_t)1 << 30 || M > ((int64_t)1 << 31) - 1 || N > ((int64_t)1 << 31) - 1) return false;
+  if ((M + BM - 1) / BM > 0xFFFF || (N + BN - 1) / BN > 0xFFFF) return false;   // 16-bit tile coordinates
   return true;
 }
 
@@ -1316,6 +1378,10 @@ static cudaError_t run_tc(const uint8_t* A, const uint8_t* B, const uint8_t* SA,
   decide_kernel<FMT><<<grid_for(tiles_m * tiles_n * nb), 256, 0, stream>>>(tiles_m, tiles_n, nb, G, T);
   tile_f32_kernel<FMT><<<grid_for(tiles_m * tiles_n), 256, 0, stream>>>(
       tiles_m, tiles_n, nb, nb == 1 ? args.stage3_rounding : args.stage4_rounding, T);
+  uint32_t* list64 = reinterpret_cast<uint32_t*>(ws + L.tile_list);
+  uint32_t* list32 = list64 + tiles_m * tiles_n;
+  uint32_t* counts = reinterpret_cast<uint32_t*>(ws + L.tile_count);
+  tile_lists_kernel<<<1, 1024, 0, stream>>>(tiles_m, tiles_n, T.tile_f32, list64, list32, counts);
   __half* af16 = reinterpret_cast<__half*>(ws + L.af16);
   __half* bf16 = reinterpret_cast<__half*>(ws + L.bf16);
   fold_rows_kernel<<<grid_for(M * K / 8), 256, 0, stream>>>(a16, M, K, GS, T.rmaq, af16);
@@ -1342,7 +1408,7 @@ static cudaError_t run_tc(const uint8_t* A, const uint8_t* B, const uint8_t* SA,
   prm.col_nan = T.col_nan;
   prm.colrec = T.colrec;
   prm.path = T.path;
-  prm.tile_f32 = T.tile_f32;
+
   prm.alpha = alpha;
   prm.out = out;
   prm.err = reinterpret_cast<int*>(ws + L.err);
@@ -1355,18 +1421,26 @@ static cudaError_t run_tc(const uint8_t* A, const uint8_t* B, const uint8_t* SA,
 
   const unsigned grid = (unsigned)std::min<int64_t>(tiles_m * tiles_n, sms);
   const int rm = nb == 1 ? args.stage3_rounding : args.stage4_rounding;
-  auto launch = [&](auto kern, int threads) -> cudaError_t {
+  // two launches over the two tile lists; a launch whose list is empty exits after its setup
+  auto launch = [&](auto kern, int which) -> cudaError_t {
     cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
     if (err != cudaSuccess) return err;
-    kern<<<grid, threads, SMEM_BYTES, stream>>>(tmA, tmB, tmAF, tmBF, tmBM, prm);
-    return cudaSuccess;
+    Params pl = prm;
+    pl.tile_list = which ? list32 : list64;
+    pl.tile_count = counts + which;
+    kern<<<grid, 32 * NUM_WARPS, SMEM_BYTES, stream>>>(tmA, tmB, tmAF, tmBF, tmBM, pl);
+    return cudaGetLastError();
+  };
+  auto launch_pair = [&](auto k64, auto k32) -> cudaError_t {
+    cudaError_t err = launch(k64, 0);
+    return err != cudaSuccess ? err : launch(k32, 1);
   };
   if (args.cmp_ref)
-    e = rm == EMU_RNE ? launch(emul_gemm_tc_kernel<FMT, EMU_RNE, true>, 32 * NUM_WARPS)
-                      : launch(emul_gemm_tc_kernel<FMT, EMU_RZ, true>, 32 * NUM_WARPS);
+    e = rm == EMU_RNE ? launch_pair(emul_gemm_tc_kernel<FMT, EMU_RNE, true, false>, emul_gemm_tc_kernel<FMT, EMU_RNE, true, true>)
+                      : launch_pair(emul_gemm_tc_kernel<FMT, EMU_RZ, true, false>, emul_gemm_tc_kernel<FMT, EMU_RZ, true, true>);
   else
-    e = rm == EMU_RNE ? launch(emul_gemm_tc_kernel<FMT, EMU_RNE, false>, 32 * NUM_WARPS)
-                      : launch(emul_gemm_tc_kernel<FMT, EMU_RZ, false>, 32 * NUM_WARPS);
+    e = rm == EMU_RNE ? launch_pair(emul_gemm_tc_kernel<FMT, EMU_RNE, false, false>, emul_gemm_tc_kernel<FMT, EMU_RNE, false, true>)
+                      : launch_pair(emul_gemm_tc_kernel<FMT, EMU_RZ, false, false>, emul_gemm_tc_kernel<FMT, EMU_RZ, false, true>);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }

@@ -73,11 +73,13 @@ __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
 }
 
 // Per-warpgroup register reallocation; every warp of the warpgroup executes the same call.
+// The "memory" clobber keeps loads from being moved above the register split (a loaded value held
+// across setmaxnreg.dec was observed to be lost).
 template <int N> __device__ __forceinline__ void setmaxnreg_dec() {
-  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N) : "memory");
 }
 template <int N> __device__ __forceinline__ void setmaxnreg_inc() {
-  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N) : "memory");
 }
 
 // ---- tcgen05
