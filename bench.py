@@ -6,9 +6,10 @@ with 1% of the K columns (the same 82 indices in A and B, seeded) scaled by 100 
 data, drawn on the CPU and moved to the GPU.  One step = the public path a caller runs per case:
 ``quant_fn(A, B)`` (device global scales + NVFP4 quantisation of both operands) then
 ``emul_fn(state)`` (the emulated GEMM, fp16 out as the reference NVFP emulator returns).
-``value`` is M*N*K per step with inputs resident in HBM; ``e2e`` adds the host->device copy of A, B
-from pinned memory and the device->host copy of the output.  Multi-GPU: every rank runs its own
-seeded case (weak scaling); timing is the max over ranks of CUDA-event time.
+``value`` is M*N*K per step with inputs resident in HBM; ``e2e`` adds, every step, the host->device
+copy of A, B from pinned memory and the device->host copy of the output, on copy streams that
+overlap the neighbouring steps' compute (double-buffered device inputs).  Multi-GPU: every rank runs
+its own seeded case (weak scaling); timing is the max over ranks of CUDA-event time.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--mnk M,N,K]
 
@@ -329,20 +330,50 @@ def main() -> int:
     ms_local = t0.elapsed_time(t1)
     gemm_ms = sum(s.elapsed_time(e) for s, e in gemm_ev) / args.steps
 
-    # ---- end to end: pinned host inputs -> device -> quant + emul -> host output
+    # ---- end to end: pinned host inputs -> device -> quant + emul -> host output, every step.  The
+    # copies run on their own streams with two device input buffers, so step i's host->device copy
+    # overlaps step i-1's compute and its device->host copy overlaps step i+1's (a serving pipeline).
     a_p, b_p = a_h.pin_memory(), b_h.pin_memory()
     out_h = torch.empty((M, N), dtype=torch.float16).pin_memory()
-    for _ in range(2):
-        _, o = step(a_p.to(dev, non_blocking=True), b_p.to(dev, non_blocking=True))
-        out_h.copy_(o, non_blocking=True)
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    a_buf = [torch.empty_like(a_d), torch.empty_like(a_d)]
+    b_buf = [torch.empty_like(b_d), torch.empty_like(b_d)]
+
+    def e2e_steps(n):
+        used = [None, None]                    # compute-done event of the step that last read buffer j
+        last_out = None
+        for i in range(n):
+            j = i % 2
+            with torch.cuda.stream(s_in):
+                if used[j] is not None:
+                    s_in.wait_event(used[j])
+                a_buf[j].copy_(a_p, non_blocking=True)
+                b_buf[j].copy_(b_p, non_blocking=True)
+                ready = torch.cuda.Event()
+                ready.record(s_in)
+            stream.wait_event(ready)
+            _, o = step(a_buf[j], b_buf[j])
+            done = torch.cuda.Event()
+            done.record(stream)
+            used[j] = done
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(done)
+                out_h.copy_(o, non_blocking=True)
+                o.record_stream(s_out)
+                last_out = torch.cuda.Event()
+                last_out.record(s_out)
+        stream.wait_event(last_out)
+
+    e2e_steps(2)
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if world > 1:
         dist.barrier()
+    torch.cuda.synchronize()
     e0.record(stream)
-    for _ in range(args.steps):
-        _, o = step(a_p.to(dev, non_blocking=True), b_p.to(dev, non_blocking=True))
-        out_h.copy_(o, non_blocking=True)
+    s_in.wait_stream(stream)
+    s_out.wait_stream(stream)
+    e2e_steps(args.steps)
     e1.record(stream)
     torch.cuda.synchronize()
     e2e_local = e0.elapsed_time(e1)

@@ -710,9 +710,12 @@ __device__ __forceinline__ void sum_update16(double (&acc)[CPT], const float (&v
 
 // f32 form of the block-sum update, the accumulator's f32 value kept in the low half of acc[]:
 // s = T * 2^e_row * 2^e_col with T = word - 1.5*2^23 (|T| < 2^22), acc = R4(acc + s) in one FMA.
-// NVFP4: T * 2^e_row = word * 2^e_row - 1.5*2^23 * 2^e_row exactly (e_row >= -10); MXFP4: 2^e_row *
-// 2^e_col is exact (a normal product when the tile pair passes the range test).
-template <int FMT, int RM, int OFF, int CPT>
+// T * 2^e_row = FMA(word, 2^e_row, -1.5*2^23 * 2^e_row) exactly while -1.5*2^23 * 2^e_row is finite
+// (e_row <= 104) -- always for NVFP4 (e_row >= -10); T * 2^e_row is a multiple of 2^e_row >= 2^-149,
+// so it is representable even when subnormal.  Otherwise (MXFP4 rows with e_row > 104) T exactly as
+// word - 1.5*2^23 and the factor 2^e_row * 2^e_col, exact for a normal product (the tile pair's
+// range test).
+template <bool ROW_FOLD, int RM, int OFF, int CPT>
 __device__ __forceinline__ void sum_update16_f32(double (&acc)[CPT], const float (&v)[16], const float* csf, float cr) {
   const float ncr = -MAGIC_F * cr;
 #pragma unroll
@@ -723,7 +726,7 @@ __device__ __forceinline__ void sum_update16_f32(double (&acc)[CPT], const float
       const float c = h == 0 ? c4.x : h == 1 ? c4.y : h == 2 ? c4.z : c4.w;
       const float a = __int_as_float(__double2loint(acc[OFF + j + h]));
       float r;
-      if (FMT == EMU_FMT_NVFP4) {
+      if (ROW_FOLD) {
         const float t = __fmaf_rn(v[j + h], cr, ncr);
         r = RM == EMU_RZ ? __fmaf_rz(t, c, a) : __fmaf_rn(t, c, a);
       } else {
@@ -1000,9 +1003,15 @@ emul_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
           __syncwarp();
           if (lane == 0) ptx::mbar_arrive(&tm_empty[set]);
           const float* csf = reinterpret_cast<const float*>(cr + CR_CSF) + col0;
-          const float crf = pow2f((int)(rs_hi >> 20) - 1075);
-          sum_update16_f32<FMT, RM, 0>(acc, v0, csf, crf);
-          if constexpr (CPT == 32) sum_update16_f32<FMT, RM, 16>(acc, v1, csf, crf);
+          const int e_row = (int)(rs_hi >> 20) - 1075;
+          const float crf = pow2f(e_row);
+          if (FMT == EMU_FMT_NVFP4 || e_row <= 104) {
+            sum_update16_f32<true, RM, 0>(acc, v0, csf, crf);
+            if constexpr (CPT == 32) sum_update16_f32<true, RM, 16>(acc, v1, csf, crf);
+          } else {
+            sum_update16_f32<false, RM, 0>(acc, v0, csf, crf);
+            if constexpr (CPT == 32) sum_update16_f32<false, RM, 16>(acc, v1, csf, crf);
+          }
         } else if (path == PATH_SUM) {
           // the row constant for words 0x4B400000 + T instead of T + 2^31 (exact: multiples of 2^e)
           const double rs_c_sum = __fma_rn(-(double)F_TO_T31 * 0x1p-52, __hiloint2double((int)rs_hi, 0), rs_c);
