@@ -971,17 +971,28 @@ emul_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
         // 24-bit rounding in f64 is exact when the accumulator provably stays in the f32 normal range
         const bool fast = (FMT == EMU_FMT_NVFP4) || (pcode & PATH_NORMAL);
         if (kb + 1 < p.nb) nx_path = path_row[kb + 1];
+        // MXFP4: records first (usually long in place), so the row record's shared-memory read
+        // overlaps the wait for the block's MMAs (NVFP4's register allocation does worse with it)
+        double2 rsv_early = make_double2(0.0, 0.0);
+        if constexpr (FMT == EMU_FMT_MXFP4) {
+          ok = __all_sync(0xFFFFFFFFu, ptx::mbar_wait(&cr_full[q], (uint32_t)((it / NCR) & 1), p.err, 6));
+          if (!ok) break;
+          rsv_early = reinterpret_cast<const double2*>(rr_ring + q * RR_BYTES + RR_RS)[rl];
+        }
         ok = __all_sync(0xFFFFFFFFu, ptx::mbar_wait(&tm_full[set], (uint32_t)((it / NSETS) & 1), p.err, 5));
         if (!ok) break;
-        ok = __all_sync(0xFFFFFFFFu, ptx::mbar_wait(&cr_full[q], (uint32_t)((it / NCR) & 1), p.err, 6));
-        if (!ok) break;
+        if constexpr (FMT != EMU_FMT_MXFP4) {
+          ok = __all_sync(0xFFFFFFFFu, ptx::mbar_wait(&cr_full[q], (uint32_t)((it / NCR) & 1), p.err, 6));
+          if (!ok) break;
+        }
         ptx::tc_fence_after();
         const uint8_t* cr = cr_ring + q * CR_BYTES;
         const int32_t* sbq = reinterpret_cast<const int32_t*>(cr + CR_SBQ);
         const uint32_t* kc = reinterpret_cast<const uint32_t*>(cr + CR_KC);
         const double* cs = reinterpret_cast<const double*>(cr + CR_CS);
         const double* sbw = reinterpret_cast<const double*>(cr + CR_SBW);
-        const double2 rsv = reinterpret_cast<const double2*>(rr_ring + q * RR_BYTES + RR_RS)[rl];
+        const double2 rsv =
+            FMT == EMU_FMT_MXFP4 ? rsv_early : reinterpret_cast<const double2*>(rr_ring + q * RR_BYTES + RR_RS)[rl];
         const uint32_t rs_hi = (uint32_t)__double2hiint(rsv.x);
         const double rs_c = rsv.y;
         const bool use32 = F32 && path == PATH_SUM && fast;
