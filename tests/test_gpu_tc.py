@@ -152,3 +152,26 @@ def test_tc_outlier_channels(kind, absval, r3, r4, out, factor):
                            w_reduce=4 if kind == "nvfp" else 2, r3=r3, r4=r4, alpha=alpha, out_mode=out)
     assert _compare(simt, ref, out) == 0
     assert _compare(got, ref, out) == 0
+
+
+@pytest.mark.parametrize("r4", [0, 1])
+def test_tc_split_launches(r4):
+    """One call whose tile pairs go to both launches: outlier channels in the first 128 rows of A and
+    the first 64 rows of B only, so tile pairs touching either keep most blocks off the block-sum path
+    (f64 launch) while the others stay on it (f32 launch).  Compared bit for bit with the oracle."""
+    from emugen_b200 import nvfp4_global_scales, quant_nvfp4
+
+    g = torch.Generator().manual_seed(101 + r4)
+    M, N, K = 256, 256, 4096
+    xa, xb = torch.randn(M, K, generator=g), torch.randn(N, K, generator=g)
+    cols = torch.randperm(K, generator=g)[:K // 50]
+    xa[:128, cols] *= 100
+    xb[:64, cols] *= 100
+    xa, xb = xa.half().cuda(), xb.half().cuda()
+    gsa, gsb, al = nvfp4_global_scales(xa, xb)
+    (qa, sfa), (qb, sfb) = quant_nvfp4(xa, gsa), quant_nvfp4(xb, gsb)
+    alpha = float(al.item())
+    a, b, sfa, sfb = qa.cpu().numpy(), qb.cpu().numpy(), sfa.cpu().numpy(), sfb.cpu().numpy()
+    got = _run(a, b, sfa, sfb, "nvfp", 0, r4, alpha, 0, "auto")
+    ref = oracle.emul_gemm(a, b, sfa, sfb, scale_fmt=0, group_size=16, w_reduce=4, r3=0, r4=r4, alpha=alpha, out_mode=0)
+    assert _compare(got, ref, 0) == 0
