@@ -192,11 +192,11 @@ __device__ __forceinline__ float pow2f(int e) {    // exact 2^e for e in [-149, 
   return e >= -126 ? __int_as_float((e + 127) << 23) : __int_as_float(1 << (e + 149));
 }
 
-// atomicMax of v over the active lanes of a warp whose lanes share `slot`
+// atomicMax of v into *slot, reduced first over the active lanes of the warp that target the same slot
 __device__ __forceinline__ void warp_atomic_max(uint32_t* slot, uint32_t v) {
-  const unsigned mask = __activemask();
-  v = __reduce_max_sync(mask, v);
-  if ((threadIdx.x & 31) == __ffs(mask) - 1) atomicMax(slot, v);
+  const unsigned peers = __match_any_sync(__activemask(), reinterpret_cast<unsigned long long>(slot));
+  v = __reduce_max_sync(peers, v);
+  if ((threadIdx.x & 31) == __ffs(peers) - 1) atomicMax(slot, v);
 }
 
 // Row base record for exponent e: x = double{hi = exponent word of 2^(52+e), lo = T + 2^31} is
@@ -208,18 +208,12 @@ __device__ __forceinline__ double2 row_base(int e) {
   return r;
 }
 
-// MXFP4: fold this thread's scale bytes into its tile's {max byte, 255 - min byte}.  The lanes of a
-// warp always belong to one tile (tiles are multiples of 32 rows / columns).
+// MXFP4: fold this thread's scale bytes into its tile's {max byte, 255 - min byte}
 __device__ __forceinline__ void scale_range(const uint32_t* byte, int n, uint32_t* rng) {
   uint32_t mx = 0, mn = 255;
   for (int g = 0; g < n; ++g) { mx = max(mx, byte[g]); mn = min(mn, byte[g]); }
-  const unsigned mask = __activemask();
-  mx = __reduce_max_sync(mask, mx);
-  mn = __reduce_min_sync(mask, mn);
-  if ((threadIdx.x & 31) == __ffs(mask) - 1) {
-    atomicMax(&rng[0], mx);
-    atomicMax(&rng[1], 255u - mn);
-  }
+  warp_atomic_max(&rng[0], mx);
+  warp_atomic_max(&rng[1], 255u - mn);
 }
 
 // one thread per (row, block)
@@ -228,8 +222,9 @@ __global__ void row_tables_kernel(const uint8_t* __restrict__ sf, int64_t M, int
                                   int64_t sf_cols, PrepTables t) {
   constexpr int GPB = Fmt<FMT>::GPB;
   const int64_t tiles_m = Mp / BM;
+  // the block index runs fastest, so a warp's per-(row, group) table writes are contiguous
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < Mp * nb; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t kb = i / Mp, r = i % Mp;
+    const int64_t r = i / nb, kb = i % nb;
     uint8_t* rec = t.rowrec + (kb * tiles_m + r / BM) * RR_BYTES;
     double2* rs = reinterpret_cast<double2*>(rec + RR_RS) + r % BM;
     if (r >= M) {   // rows of the last tile beyond M: finite, discarded by the epilogue
@@ -534,12 +529,12 @@ __global__ void decide_kernel(int64_t tiles_m, int64_t tiles_n, int64_t nb, int6
     // (NVFP4 only: MXFP4 blocks rarely miss the block-sum path and its epilogue keeps one path less)
     const bool mixed = FMT == EMU_FMT_NVFP4 && ok && fold_rest && (fmin(fmin(r1, r2), r3) < 4194304.0);
     uint8_t code = sum ? PATH_SUM : mixed ? (uint8_t)(PATH_MIXED | (gx << PATH_GROUP_SHIFT)) : (ok ? PATH_INT : PATH_F64);
+    float sabs = 0.0f;
     if (FMT == EMU_FMT_NVFP4) {
       code |= PATH_NORMAL;   // |acc| < 2^40 and every term a multiple of 2^-20: always in range
       // |s_b| <= tb * 2^(row base + column base - 2) for every output of the tile pair
       const int eb = (int)t.rbmax[tm * nb + kb] + (int)t.cbmax[tn * nb + kb] - 1024 - 2;
-      const float sabs = ok ? (float)(tb * margin * pow2d(eb)) : __int_as_float(0x7F800000);
-      atomicAdd(&t.tile_bound[tm * tiles_n + tn], sabs);
+      sabs = ok ? (float)(tb * margin * pow2d(eb)) : __int_as_float(0x7F800000);
     } else {
       // every block term is a multiple of 2^(minA + minB - 256) and at most 9216 * 2^(maxA + maxB - 256):
       // no accumulator value is subnormal or reaches 2^127 when these hold for the whole tile pair
@@ -549,7 +544,22 @@ __global__ void decide_kernel(int64_t tiles_m, int64_t tiles_n, int64_t nb, int6
         code |= PATH_NORMAL;
     }
     t.path[i] = code;
-    if ((code & 3) != PATH_SUM) atomicAdd(&t.tile_other[tm * tiles_n + tn], 1u);
+    // per tile pair: the sum of the block bounds and the count of blocks off the block-sum path.  When
+    // nb is a multiple of 32 every warp (32-aligned, every lane active) covers blocks of one tile pair
+    // and reduces before its single pair of atomics.
+    const bool other = (code & 3) != PATH_SUM;
+    if ((nb & 31) == 0) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) sabs += __shfl_xor_sync(0xFFFFFFFFu, sabs, o);
+      const unsigned n_other = __popc(__ballot_sync(0xFFFFFFFFu, other));
+      if ((threadIdx.x & 31) == 0) {
+        if (FMT == EMU_FMT_NVFP4) atomicAdd(&t.tile_bound[tm * tiles_n + tn], sabs);
+        if (n_other) atomicAdd(&t.tile_other[tm * tiles_n + tn], n_other);
+      }
+    } else {
+      if (FMT == EMU_FMT_NVFP4) atomicAdd(&t.tile_bound[tm * tiles_n + tn], sabs);
+      if (other) atomicAdd(&t.tile_other[tm * tiles_n + tn], 1u);
+    }
   }
 }
 

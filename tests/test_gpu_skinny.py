@@ -80,3 +80,38 @@ def test_decode_shape_timing_smoke():
         ref = oracle.emul_gemm(a, b[cols], saz, swizzle(sb[cols], 128, pad(G, 4)), scale_fmt=0, group_size=16,
                                w_reduce=4, alpha=None, out_mode=0)
         assert nan_equal_mismatches(_bits(got)[:, cols], ref, "float16") == 0
+
+
+@pytest.mark.parametrize("kind", ["nvfp", "mxfp"])
+@pytest.mark.parametrize("M,N", [(0, 64), (64, 0), (0, 0), (1, 1)])
+def test_degenerate_shapes(kind, M, N):
+    """Empty and single-output problems through the C ABI: an empty output is returned without a launch
+    failure, a 1x1 output matches the oracle."""
+    from emugen_b200 import _lib
+    from tests.golden.make_golden import pad, swizzle
+
+    K = 128
+    gs = 16 if kind == "nvfp" else 32
+    G = K // gs
+    rng = np.random.default_rng(M * 131 + N + (7 if kind == "mxfp" else 0))
+    a = rng.integers(0, 256, size=(M, K // 2), dtype=np.uint8)
+    b = rng.integers(0, 256, size=(N, K // 2), dtype=np.uint8)
+    if kind == "nvfp":
+        sa = rng.integers(0x20, 0x50, size=(max(M, 1), G), dtype=np.uint8)
+        sb = rng.integers(0x20, 0x50, size=(max(N, 1), G), dtype=np.uint8)
+    else:
+        sa = rng.integers(120, 135, size=(max(M, 1), G), dtype=np.uint8)
+        sb = rng.integers(120, 135, size=(max(N, 1), G), dtype=np.uint8)
+    sfa = swizzle(sa, pad(max(M, 1), 128), pad(G, 4))
+    sfb = swizzle(sb, pad(max(N, 1), 128), pad(G, 4))
+    alpha = 0.5 if kind == "nvfp" else None
+    al = None if alpha is None else torch.tensor([alpha], dtype=torch.float32, device="cuda")
+    got = _lib.gemm(torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda(), torch.from_numpy(sfa).cuda(),
+                    torch.from_numpy(sfb).cuda(), fmt=0 if kind == "nvfp" else 1, group_size=gs,
+                    w_reduce=4 if kind == "nvfp" else 2, stage3_rounding=0, stage4_rounding=0, alpha=al, out_mode=0)
+    torch.cuda.synchronize()
+    assert tuple(got.shape) == (M, N)
+    if M and N:
+        ref = oracle.emul_gemm(a, b, sfa, sfb, scale_fmt=0 if kind == "nvfp" else 1, group_size=gs,
+                               w_reduce=4 if kind == "nvfp" else 2, alpha=alpha, out_mode=0)
+        assert nan_equal_mismatches(_bits(got), ref, "float16") == 0
