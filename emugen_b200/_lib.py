@@ -24,7 +24,7 @@ EMU_OUT_F16, EMU_OUT_BF16_VIA_F16, EMU_OUT_F32 = 0, 1, 2
 EMU_DTYPE_F16, EMU_DTYPE_BF16, EMU_DTYPE_F32 = 0, 1, 2
 ABI_VERSION = 1
 
-SYMBOLS = ("emu_abi_version", "emu_last_error", "emu_status_string", "emu_gemm", "emu_gemm_workspace_size",
+SYMBOLS = ("emu_abi_version", "emu_last_error", "emu_status_string", "emu_gemm", "emu_gemm_workspace_size", "emu_gemm_tc_workspace_size",
            "emu_gemm_ws", "emu_gemm_static", "emu_nvfp4_global_scales", "emu_quant_nvfp4", "emu_quant_mxfp4",
            "emu_gemm_model", "emu_gemm_compare", "emu_compare", "emu_dequant_fp4")
 STATIC_SCRATCH_BYTES = 64 << 20   # EMU_STATIC_SCRATCH_BYTES
@@ -82,6 +82,8 @@ def load() -> ctypes.CDLL:
                                ctypes.POINTER(EmuGemmParams), vp, vp]
         L.emu_gemm_workspace_size.restype = ctypes.c_size_t
         L.emu_gemm_workspace_size.argtypes = [i64, i64, i64, ctypes.POINTER(EmuGemmParams)]
+        L.emu_gemm_tc_workspace_size.restype = ctypes.c_size_t
+        L.emu_gemm_tc_workspace_size.argtypes = [i64, i64, i64, ctypes.POINTER(EmuGemmParams)]
         L.emu_gemm_ws.restype = i32
         L.emu_gemm_ws.argtypes = [vp, vp, vp, vp, i64, i64, i64, i64, i64, i64, i64, vp,
                                   ctypes.POINTER(EmuGemmParams), vp, vp, ctypes.c_size_t, vp]
@@ -144,8 +146,10 @@ def gemm(a_fp4: torch.Tensor, b_fp4: torch.Tensor, scale_a: torch.Tensor, scale_
     """Emulated scaled FP4 GEMM through ``emu_gemm_ws``.  Returns [M, N] fp16 / bf16 / f32 on the
     inputs' CUDA device (or on CPU if every input was on CPU).
 
-    path: "auto" gives the library a workspace (tensor-core kernel where it applies); "simt" passes
-    none, which selects the CUDA-core kernel.  Both are bit-identical; "simt" exists for tests."""
+    path: "auto" gives the library the workspace it asks for (the tensor-core kernel where it applies
+    and the problem is large enough to gain from it); "tc" gives the tensor-core kernel's workspace
+    whatever the size; "simt" passes none, which selects the CUDA-core kernels.  All are bit-identical;
+    "tc" and "simt" exist for tests."""
     L = load()
     on_cpu = not any(t.is_cuda for t in (a_fp4, b_fp4, scale_a, scale_b))
     dev = _device_for(a_fp4, b_fp4, scale_a, scale_b)
@@ -169,13 +173,14 @@ def gemm(a_fp4: torch.Tensor, b_fp4: torch.Tensor, scale_a: torch.Tensor, scale_
     out = torch.empty((M, N), dtype=odt, device=dev)
     params = EmuGemmParams(fmt, group_size, w_reduce, stage3_rounding, stage4_rounding, out_mode)
     ws_ptr, ws_bytes, ws = None, 0, None
-    if path == "auto" and M > 0 and N > 0 and K > 0:
-        need = L.emu_gemm_workspace_size(M, N, K, ctypes.byref(params))
+    if path in ("auto", "tc") and M > 0 and N > 0 and K > 0:
+        query = L.emu_gemm_workspace_size if path == "auto" else L.emu_gemm_tc_workspace_size
+        need = query(M, N, K, ctypes.byref(params))
         if need:
             ws = torch.empty(need + 1024, dtype=torch.uint8, device=dev)
             ws_ptr = (ws.data_ptr() + 1023) // 1024 * 1024
             ws_bytes = need
-    elif path not in ("auto", "simt"):
+    elif path not in ("auto", "tc", "simt"):
         raise ValueError(f"unknown path {path!r}")
     with torch.cuda.device(dev):
         st = L.emu_gemm_ws(a.data_ptr(), b.data_ptr(), sa.data_ptr(), sb.data_ptr(), M, N, K,
@@ -313,8 +318,9 @@ def gemm_compare(a_fp4: torch.Tensor, b_fp4: torch.Tensor, scale_a: torch.Tensor
     al = None if alpha is None else alpha.detach().reshape(1).to(device=dev, dtype=torch.float32).contiguous()
     params = EmuGemmParams(fmt, group_size, w_reduce, stage3_rounding, stage4_rounding, out_mode)
     ws_ptr, ws_bytes, ws = None, 0, None
-    if path == "auto":
-        need = L.emu_gemm_workspace_size(M, N, K, ctypes.byref(params))
+    if path in ("auto", "tc"):
+        query = L.emu_gemm_workspace_size if path == "auto" else L.emu_gemm_tc_workspace_size
+        need = query(M, N, K, ctypes.byref(params))
         if need:
             ws = torch.empty(need + 1024, dtype=torch.uint8, device=dev)
             ws_ptr = (ws.data_ptr() + 1023) // 1024 * 1024

@@ -114,11 +114,27 @@ static bool tc_path(const emu_gemm_params& p, int64_t M, int64_t N, int64_t K) {
   return emu::gemm_tc_supported(p.format, p.w_reduce, M, N, K);
 }
 
-size_t emu_gemm_workspace_size(int64_t M, int64_t N, int64_t K, const emu_gemm_params* params) {
+// Problems below these sizes finish sooner on the CUDA-core kernels than through the tensor-core
+// kernel's pre-pass and two launches (B200: NVFP4 128x128x256 30 us vs 95 us, 512x512x1024 101 vs
+// 109 us; MXFP4 1024^3 76 vs 133 us, 1024x1024x2048 148 vs 144 us).
+static bool tc_preferred(const emu_gemm_params& p, int64_t M, int64_t N, int64_t K) {
+  const double macs = (double)M * (double)N * (double)K;
+  return tc_path(p, M, N, K) && macs >= (p.format == EMU_FMT_NVFP4 ? 0x1p27 : 0x1p30);
+}
+
+static size_t workspace_for(int64_t M, int64_t N, int64_t K, const emu_gemm_params* params, bool prefer) {
   if (!params || M <= 0 || N <= 0 || K <= 0) return 0;
   if (params->group_size <= 0 || K % params->group_size != 0) return 0;
-  if (!tc_path(*params, M, N, K)) return 0;
+  if (!(prefer ? tc_preferred(*params, M, N, K) : tc_path(*params, M, N, K))) return 0;
   return emu::gemm_tc_workspace_size(params->format, M, N, K);
+}
+
+size_t emu_gemm_workspace_size(int64_t M, int64_t N, int64_t K, const emu_gemm_params* params) {
+  return workspace_for(M, N, K, params, true);
+}
+
+size_t emu_gemm_tc_workspace_size(int64_t M, int64_t N, int64_t K, const emu_gemm_params* params) {
+  return workspace_for(M, N, K, params, false);
 }
 
 emu_status emu_gemm_ws(const uint8_t* a_fp4, const uint8_t* b_fp4, const uint8_t* scale_a, const uint8_t* scale_b,

@@ -105,9 +105,18 @@ EMU_API emu_status emu_gemm(const uint8_t* a_fp4, const uint8_t* b_fp4, const ui
 /*
  * Bytes of device workspace emu_gemm_ws needs to take the tensor-core path for this problem
  * (0 when the problem runs on the CUDA-core path, which needs none).  The tensor-core path covers
- * the reference's accumulator shapes (NVFP4 w_reduce 4, MXFP4 w_reduce 2) with K a multiple of 64.
+ * the reference's accumulator shapes (NVFP4 w_reduce 4, MXFP4 w_reduce 2) with K a multiple of 64;
+ * problems below 2^27 (NVFP4) / 2^30 (MXFP4) multiply-accumulates return 0 here because the CUDA-core
+ * kernels finish them sooner.
  */
 EMU_API size_t emu_gemm_workspace_size(int64_t M, int64_t N, int64_t K, const emu_gemm_params* params);
+
+/*
+ * The tensor-core path's workspace for this problem whatever its size (0 where that path does not
+ * apply): a workspace of this size passed to emu_gemm_ws selects the tensor-core kernel even for
+ * small problems.  No reference counterpart (a kernel choice the reference does not have).
+ */
+EMU_API size_t emu_gemm_tc_workspace_size(int64_t M, int64_t N, int64_t K, const emu_gemm_params* params);
 
 /*
  * emu_gemm with caller-provided scratch: `workspace` (1024-byte aligned, at least

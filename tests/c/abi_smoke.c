@@ -63,7 +63,7 @@ int main(void) {
   emu_gemm_params p = {EMU_FMT_NVFP4, 16, 4, EMU_RZ, EMU_RZ, EMU_OUT_F16};
   CHECK(emu_gemm((const uint8_t*)qa, (const uint8_t*)qb, (const uint8_t*)sa, (const uint8_t*)sb, M, N, K, sf_rows_a,
                  sf_cols, sf_rows_b, sf_cols, alpha, &p, out1, NULL));
-  size_t need = emu_gemm_workspace_size(M, N, K, &p);
+  size_t need = emu_gemm_tc_workspace_size(M, N, K, &p);   /* the tensor-core kernel at this small shape */
   if (need == 0) { fprintf(stderr, "expected the tensor-core path at this shape\n"); return 1; }
   CUDA(cudaMalloc(&ws, need + 1024));
   void* ws_al = (void*)(((uintptr_t)ws + 1023) & ~(uintptr_t)1023);

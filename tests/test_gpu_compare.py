@@ -187,7 +187,7 @@ def test_fused_gemm_compare_matches_separate_compare(kind, out_mode):
     flat[7] = flat[7] * 2 + 1
     flat[1000] = float("nan")
     flat[5000] = -flat[5000] if flat[5000] != 0 else 1.0
-    for path in ("auto", "simt"):
+    for path in ("tc", "simt"):
         for write_out in (False, True):
             st, o = _lib.gemm_compare(*t, ref, path=path, write_out=write_out, **kw)
             want = _lib.compare_stats(ref, out)

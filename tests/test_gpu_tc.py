@@ -65,8 +65,8 @@ def test_tc_vs_oracle_and_simt(case):
                                 case["r3"], case["r4"], case["out"])
     import ctypes
 
-    assert _lib.load().emu_gemm_workspace_size(case["M"], case["N"], case["K"], ctypes.byref(params)) > 0
-    got = _run(a, b, sfa, sfb, kind, case["r3"], case["r4"], alpha, case["out"], "auto")
+    assert _lib.load().emu_gemm_tc_workspace_size(case["M"], case["N"], case["K"], ctypes.byref(params)) > 0
+    got = _run(a, b, sfa, sfb, kind, case["r3"], case["r4"], alpha, case["out"], "tc")
     simt = _run(a, b, sfa, sfb, kind, case["r3"], case["r4"], alpha, case["out"], "simt")
     ref = oracle.emul_gemm(a, b, sfa, sfb, scale_fmt=0 if kind == "nvfp" else 1, group_size=16 if kind == "nvfp" else 32,
                            w_reduce=4 if kind == "nvfp" else 2, r3=case["r3"], r4=case["r4"], alpha=alpha,
@@ -94,7 +94,7 @@ def test_tc_8192_sampled_against_oracle():
     qb, sfb = quant_nvfp4(xb, gsb)
     a, b, sfa, sfb = qa.cpu().numpy(), qb.cpu().numpy(), sfa.cpu().numpy(), sfb.cpu().numpy()
     al = float(alpha.item())
-    got = _bits(_run(a, b, sfa, sfb, "nvfp", 0, 0, al, 0, "auto"))
+    got = _bits(_run(a, b, sfa, sfb, "nvfp", 0, 0, al, 0, "tc"))
     rng = np.random.default_rng(5)
     rows = rng.choice(M, 8, replace=False)
     cs = rng.choice(N, 8, replace=False)
@@ -146,7 +146,7 @@ def test_tc_outlier_channels(kind, absval, r3, r4, out, factor):
         (qa, sfa), (qb, sfb) = quant_mxfp4(xa), quant_mxfp4(xb)
         alpha = None
     a, b, sfa, sfb = qa.cpu().numpy(), qb.cpu().numpy(), sfa.cpu().numpy(), sfb.cpu().numpy()
-    got = _run(a, b, sfa, sfb, kind, r3, r4, alpha, out, "auto")
+    got = _run(a, b, sfa, sfb, kind, r3, r4, alpha, out, "tc")
     simt = _run(a, b, sfa, sfb, kind, r3, r4, alpha, out, "simt")
     ref = oracle.emul_gemm(a, b, sfa, sfb, scale_fmt=0 if kind == "nvfp" else 1, group_size=16 if kind == "nvfp" else 32,
                            w_reduce=4 if kind == "nvfp" else 2, r3=r3, r4=r4, alpha=alpha, out_mode=out)
@@ -172,6 +172,6 @@ def test_tc_split_launches(r4):
     (qa, sfa), (qb, sfb) = quant_nvfp4(xa, gsa), quant_nvfp4(xb, gsb)
     alpha = float(al.item())
     a, b, sfa, sfb = qa.cpu().numpy(), qb.cpu().numpy(), sfa.cpu().numpy(), sfb.cpu().numpy()
-    got = _run(a, b, sfa, sfb, "nvfp", 0, r4, alpha, 0, "auto")
+    got = _run(a, b, sfa, sfb, "nvfp", 0, r4, alpha, 0, "tc")
     ref = oracle.emul_gemm(a, b, sfa, sfb, scale_fmt=0, group_size=16, w_reduce=4, r3=0, r4=r4, alpha=alpha, out_mode=0)
     assert _compare(got, ref, 0) == 0

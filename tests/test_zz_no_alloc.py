@@ -58,7 +58,7 @@ def _run(entry, a, b, sfa, sfb, M, N, K, alpha, prm, out_dtype):
 # A larger NVFP4 problem with NaN block scales (sets the NaN row / column flags in the scratch),
 # then a smaller MXFP4 one without: the second call must not see the first call's flags.
 CASES = [dict(kind="nvfp", data="raw_nan_scales", M=384, N=320, K=2048, r3=0, r4=1, out=0),
-         dict(kind="mxfp", data="normal", M=256, N=192, K=1024, r3=1, r4=0, out=1)]
+         dict(kind="mxfp", data="normal", M=1024, N=1024, K=1024, r3=1, r4=0, out=1)]
 
 
 @pytest.mark.gpu
