@@ -270,7 +270,9 @@ def run_workload(args) -> int:
     c5   MXFP4 8192^3 ~N(0,1), bf16: the accumulator-model GEMM under 56 configurations (alignment width
          24..31 x {RZ, RNE} alignment rounding x accumulate size {32, 64, 128}, plus 8 summation orders),
          each compared on the device with the hardware FP4 GEMM (flashinfer) -- mismatch counts (the model's
-         f32 result rounded once to bf16, as the hardware's epilogue rounds)."""
+         f32 result rounded once to bf16, as the hardware's epilogue rounds).  Under torchrun the
+         configurations are split over the ranks (emugen_b200.sweep.run_sweep_sharded: one broadcast of
+         the case, one all_reduce of the counts); time = max over ranks."""
     import torch
 
     from emugen_b200 import _lib
@@ -355,47 +357,54 @@ def run_workload(args) -> int:
                              "GB_per_s": byts / (ms / 1e3) / 1e9})
         print(json.dumps({"workload": "c4 NVFP4 decode shapes, emul_fn", "shapes": rows}))
     elif w == "c5":
-        from emugen_b200 import quant_mxfp4
+        from emugen_b200 import quant_mxfp4, sweep
 
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        if world > 1:
+            import torch.distributed as dist
+            from datetime import timedelta
+
+            dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
         S = 8192
-        g = torch.Generator(device=dev).manual_seed(SEED)
-        a = torch.randn(S, S, generator=g, device=dev).bfloat16()
-        b = torch.randn(S, S, generator=g, device=dev).bfloat16()
-        (qa, sa), (qb, sb) = quant_mxfp4(a), quant_mxfp4(b)
-        try:
-            import flashinfer
+        case, real, versus = None, None, None
+        if rank == 0:
+            g = torch.Generator(device=dev).manual_seed(SEED)
+            a = torch.randn(S, S, generator=g, device=dev).bfloat16()
+            b = torch.randn(S, S, generator=g, device=dev).bfloat16()
+            (qa, sa), (qb, sb) = quant_mxfp4(a), quant_mxfp4(b)
+            try:
+                import flashinfer
 
-            real = flashinfer.gemm.mm_fp4(a=qa, b=qb.T, a_descale=sa, b_descale=sb.T, out_dtype=torch.bfloat16,
-                                          block_size=32, use_nvfp4=False, backend="cudnn")
-            versus = "flashinfer mm_fp4 (hardware FP4 GEMM)"
-        except Exception as e:  # no hardware GEMM available: compare with the exact emulation instead
-            real = _lib.gemm(qa, qb, sa, sb, fmt=1, group_size=32, w_reduce=2, stage3_rounding=0, stage4_rounding=0,
-                             alpha=None, out_mode=1)
-            versus = f"exact emulation ({type(e).__name__})"
-        cfgs = [dict(w_reduce=wr, align3=wd, align4=wd, align_rounding=rr, order=0)
-                for wd in range(24, 32) for rr in (0, 1) for wr in (1, 2, 4)]
-        cfgs += [dict(w_reduce=wr, align3=0, align4=0, align_rounding=0, order=o, r4=r4)
-                 for o in (1, 2) for wr in (2, 4) for r4 in (0, 1)]
+                real = flashinfer.gemm.mm_fp4(a=qa, b=qb.T, a_descale=sa, b_descale=sb.T, out_dtype=torch.bfloat16,
+                                              block_size=32, use_nvfp4=False, backend="cudnn")
+                versus = "flashinfer mm_fp4 (hardware FP4 GEMM)"
+            except Exception as e:  # no hardware GEMM available: compare with the exact emulation instead
+                real = _lib.gemm(qa, qb, sa, sb, fmt=1, group_size=32, w_reduce=2, stage3_rounding=0,
+                                 stage4_rounding=0, alpha=None, out_mode=1)
+                versus = f"exact emulation ({type(e).__name__})"
+            case = sweep.SweepCase(qa, qb, sa, sb, _lib.EMU_FMT_MXFP4)
+        cfgs = sweep.default_configs()
         torch.cuda.synchronize()
-        res = []
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        if world > 1:
+            dist.barrier()
         e0.record()
-        for c in cfgs:
-            # f32 accumulator of the model, rounded to bf16 once as the hardware's epilogue does (the
-            # reference's fp16 -> bf16 output path would add the same double-rounding mismatches to
-            # every configuration)
-            out = _lib.gemm_model(qa, qb, sa, sb, fmt=1, group_size=32, w_reduce=c["w_reduce"], stage3_rounding=0,
-                                  stage4_rounding=c.get("r4", 0), alpha=None, out_mode=2, align3=c["align3"],
-                                  align4=c["align4"], align_rounding=c["align_rounding"], order=c["order"])
-            res.append(_lib.compare_stats(real, out.bfloat16()))
+        mism = sweep.run_sweep_sharded(case, real, cfgs) if world > 1 else sweep.run_sweep(case, real, cfgs)
         e1.record()
         torch.cuda.synchronize()
         ms = e0.elapsed_time(e1)
-        mism = [r["mismatches"] for r in res]
-        print(json.dumps({"workload": "c5 MXFP4 8192^3 accumulator-model sweep, %d configs" % len(cfgs),
-                          "versus": versus, "ms_total": ms, "ms_per_config": ms / len(cfgs),
-                          "MAC_per_s": len(cfgs) * S ** 3 / (ms / 1e3), "mismatches_min": min(mism),
-                          "mismatches_max": max(mism), "mismatches": mism}))
+        if world > 1:
+            t = torch.tensor([ms], dtype=torch.float64, device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+            dist.destroy_process_group()
+        if rank == 0:
+            print(json.dumps({"workload": "c5 MXFP4 8192^3 accumulator-model sweep, %d configs on %d GPU(s)"
+                                          % (len(cfgs), world),
+                              "versus": versus, "ms_total": ms, "ms_per_config": ms / len(cfgs) * world,
+                              "MAC_per_s": len(cfgs) * S ** 3 / (ms / 1e3), "mismatches_min": min(mism),
+                              "mismatches_max": max(mism), "mismatches": mism}))
     return 0
 
 
