@@ -550,6 +550,14 @@ def main() -> int:
                 cpu = cpu_baseline(sc)
             except Exception as e:  # reported, not fatal
                 cpu = {"value": None, "error": f"{type(e).__name__}: {e}"}
+        # the other floor of this kernel: its stage-4 chain, one DADD + one DFMA per output and 64-wide K
+        # block on the CUDA cores (FP64 pipe: 64 results per clock per SM, measured on this B200 with a
+        # DADD-only microbenchmark), at the median SM clock sampled during the timed region
+        clk_s = clk.summary()
+        mhz = clk_s.get("sm_mhz") or clk_s.get("sm_max_mhz") or 1965
+        n_sm = torch.cuda.get_device_properties(dev).multi_processor_count
+        fp64_ops = 2.0 * macs / 64
+        fp64_floor_ms = fp64_ops / (64.0 * n_sm * mhz * 1e6) * 1e3
         line = {
             "metric": "emulated FP4 GEMM MAC/s at 8192^3" if (M, N, K) == (8192, 8192, 8192)
                       else f"emulated FP4 GEMM MAC/s at {M}x{N}x{K} (profiling size)",
@@ -566,7 +574,10 @@ def main() -> int:
                          "frac": achieved / peak, "traffic": ncu_traffic() if (M, N, K) == (8192, 8192, 8192) else None,
                          "kernel": "emul_fn launches (pre-pass kernels + emul_gemm_tc_kernel), CUDA events",
                          "kernel_ms": gemm_max, "work_per_launch": "2*M*N*K stage-1 tensor-core flops",
-                         "peak_kind": f"bf16 dense burst, {pk_kind}"},
+                         "peak_kind": f"bf16 dense burst, {pk_kind}",
+                         "cuda_core": {"what": "stage-4 chain: DADD + DFMA per output and K block, FP64 pipe",
+                                       "fp64_ops": fp64_ops, "peak_ops_per_s": 64.0 * n_sm * mhz * 1e6,
+                                       "floor_ms": fp64_floor_ms, "frac": fp64_floor_ms / gemm_max}},
             "gpu_launches": None if launches_per_step is None else launches_per_step * args.steps,
             "clocks": clk.summary(),
         }

@@ -12,13 +12,17 @@
 //                   bases; row and column records are laid out per (block, tile) so one bulk copy
 //                   each brings a block's row and column data into shared memory.
 //   tile stats      per (128-row | 64-column tile, group) maxima of the norms and multipliers.
-//   decide          per (row tile, column tile, block): block-sum, integer or f64 path (below).
-//   fold rows/cols  the operands times their group multipliers, for the block-sum / integer paths.
+//   decide          per (row tile, column tile, block): block-sum, mixed, integer or f64 path (below).
+//   tile f32/lists  per tile pair: may its block-sum updates run in f32 (exactness bound, share of
+//                   blocks off the block-sum path); the tile pairs split into two lists by that flag.
+//   fold rows/cols  the operands times their group multipliers, for the block-sum / mixed / integer
+//                   paths (B twice: every group folded, and all but the mixed path's separate group).
 //
-// Main kernel: persistent, one CTA per SM, 12 warps:
+// Main kernel: persistent, one CTA per SM, 12 warps, launched once per tile list (F32 = 0 / 1):
 //   warp 0      producer: TMA A [128 x 64] and B [64 x 64] fp16 tiles (128-byte swizzle; the folded
-//               or raw operand per the block's path) into a 6-stage ring; bulk copies of the
-//               block's column and row records into a 4-stage ring.
+//               or raw operand per the block's path) into a 6-stage ring, the block's path code in a
+//               shared byte per stage; bulk copies of the block's column and row records into an
+//               8-slot ring.
 //   warp 1      TMEM owner + MMA issuer (tcgen05.mma kind::f16 M128 N64 K16): the block-sum path
 //               into one accumulator, the other paths one accumulator per group.  512 columns = a
 //               ring of K-block sets (NVFP4: 2 sets of 4 x 64; MXFP4: 4 sets of 2 x 64).
@@ -29,7 +33,9 @@
 //     writing 1.5*2^23 and the block's four K16 MMAs into ONE accumulator: its f32 word is exactly
 //     0x4B400000 + T, T = sum_g p4_g * ma'_g * mb'_g.  Epilogue per output and block:
 //     Tf = double{2^(52+e_row), T + 2^31} - (2^52 + 2^31) * 2^e_row = T * 2^e_row,
-//     acc = R4(FMA(Tf, 2^e_col, acc)).
+//     acc = R4(FMA(Tf, 2^e_col, acc));  in the F32 launch acc = R4(FFMA(T * 2^e_row, 2^e_col, acc)) in f32.
+// Mixed path (NVFP4): the block-sum path over all groups but one, that group's B left unscaled in its
+//     own accumulator (an integer-path word): T = (w0 - bias) + (w1 - bias) * mb'.  Then as above.
 // Integer path: A folded, B raw, one accumulator per group started from the 1.5*2^23 bias, so each
 //     word is 0x4B400000 + p4 * ma'; S32 = sum_g word * mb'_g wraps in int32 and a per-column
 //     constant removes the bias terms: S32 + K_col = T + 2^31.  Then as above.
