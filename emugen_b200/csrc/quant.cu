@@ -20,6 +20,7 @@
 #include <stdint.h>
 
 #include <algorithm>
+#include <type_traits>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -139,15 +140,32 @@ quant_fp4_kernel(const T* __restrict__ x, int64_t M, int64_t K, const float* __r
 }
 
 // max |x| as float bits (non-negative floats order like their bit patterns; NaN sorts above inf,
-// so a NaN anywhere wins, as torch.max propagates NaN).
+// so a NaN anywhere wins, as torch.max propagates NaN).  The same holds for the 16-bit patterns of
+// fp16 / bf16 magnitudes, so the maximum is taken on those, two per 32-bit lane (16-byte loads), and
+// converted to float once per thread (the conversion is monotonic, so the result is the same).
+template <typename T>
+__device__ __forceinline__ unsigned half_bits_to_float_bits(unsigned h) {
+  if constexpr (std::is_same<T, __half>::value) return __float_as_uint(__half2float(__ushort_as_half((unsigned short)h)));
+  else return h << 16;
+}
+
 template <typename T>
 __global__ void amax_bits_kernel(const T* __restrict__ x, int64_t n, unsigned* __restrict__ out) {
-  unsigned m = 0;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-    float f = (float)x[i];
-    unsigned b = __float_as_uint(f) & 0x7FFFFFFFu;
-    m = max(m, b);
+  unsigned m2 = 0;   // two 16-bit magnitude maxima
+  const int64_t n8 = (reinterpret_cast<uintptr_t>(x) & 15) == 0 ? n / 8 : 0;
+  const uint4* x8 = reinterpret_cast<const uint4*>(x);
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n8; i += stride) {
+    const uint4 w = __ldg(x8 + i);
+    m2 = __vmaxu2(m2, w.x & 0x7FFF7FFFu);
+    m2 = __vmaxu2(m2, w.y & 0x7FFF7FFFu);
+    m2 = __vmaxu2(m2, w.z & 0x7FFF7FFFu);
+    m2 = __vmaxu2(m2, w.w & 0x7FFF7FFFu);
   }
+  const unsigned short* xs = reinterpret_cast<const unsigned short*>(x);
+  for (int64_t i = n8 * 8 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += stride)
+    m2 = __vmaxu2(m2, (unsigned)xs[i] & 0x7FFFu);
+  unsigned m = half_bits_to_float_bits<T>(max(m2 & 0xFFFFu, m2 >> 16));
   for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
   if ((threadIdx.x & 31) == 0) atomicMax(out, m);
 }

@@ -110,3 +110,30 @@ def test_global_scales_match_reference_recipe():
     z = torch.zeros(4, 16, dtype=torch.bfloat16, device="cuda")
     gz, _, _ = nvfp4_global_scales(z, z)
     assert gz.item() == 2688.0
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_global_scales_vector_and_tail_paths(dtype):
+    """The amax reads 16-byte vectors where the pointer allows and single elements elsewhere: a numel
+    that is not a multiple of 8, a pointer one element past a 16-byte boundary, the maximum in the
+    tail, an infinity and a NaN all give the reference's scale (gemm_compare/backends/nvfp.py:24-27)."""
+    from emugen_b200 import nvfp4_global_scales
+
+    def want(x):
+        am = torch.abs(x.float()).max().item()
+        return np.float32(448.0 * 6.0 / (am if am > 0 else 1.0))
+
+    base = torch.randn(4099, dtype=torch.float32).to(dtype).cuda()
+    for x in (base[:4097], base[1:4098]):
+        y = x.clone() if x.data_ptr() % 16 == 0 else x
+        y[-1] = 9.0
+        g, _, _ = nvfp4_global_scales(y, y)
+        w = want(y.cpu())
+        assert g.item() == float(w), (dtype, y.data_ptr() % 16)
+    z = base[:4096].clone()
+    z[77] = -float("inf")
+    g, _, _ = nvfp4_global_scales(z, z)
+    assert g.item() == float(want(z.cpu())) == 0.0          # 2688 / inf
+    z[100] = float("nan")
+    g, _, _ = nvfp4_global_scales(z, z)
+    assert g.item() == float(want(z.cpu())) == 2688.0       # NaN > 0 is false: the reference falls back to 1.0
