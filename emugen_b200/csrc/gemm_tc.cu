@@ -15,8 +15,9 @@
 //   decide          per (row tile, column tile, block): block-sum, mixed, integer or f64 path (below).
 //   tile f32/lists  per tile pair: may its block-sum updates run in f32 (exactness bound, share of
 //                   blocks off the block-sum path); the tile pairs split into two lists by that flag.
-//   fold rows/cols  the operands times their group multipliers, for the block-sum / mixed / integer
-//                   paths (B twice: every group folded, and all but the mixed path's separate group).
+//   fold            the operands times their group multipliers, for the block-sum / mixed / integer
+//                   paths: A within its unpack pass, B after the tile stats (twice: every group
+//                   folded, and all but the mixed path's separate group).
 //
 // Main kernel: persistent, one CTA per SM, 12 warps, launched once per tile list (F32 = 0 / 1):
 //   warp 0      producer: TMA A [128 x 64] and B [64 x 64] fp16 tiles (128-byte swizzle; the folded
@@ -109,10 +110,14 @@ template <> struct Fmt<EMU_FMT_NVFP4> { static constexpr int GS = 16, GPB = 4; }
 template <> struct Fmt<EMU_FMT_MXFP4> { static constexpr int GS = 32, GPB = 2; };
 
 // ------------------------------------------------------------------------------ pre-pass
-// One thread per 16 elements.  For 32-element groups the two halves sit in adjacent lanes.
-template <int GS>
+// One thread per 16 elements.  For 32-element groups the two halves sit in adjacent lanes.  FOLD
+// (the A operand): also writes the block-sum / mixed / integer paths' operand, the "2x" values times
+// their row-group multiplier `mult` (ma * 2^(e_g - e)) in fp16 -- exact wherever a block passes the
+// decide test (|product| <= 65504, at most 6 significant bits); other values are never read.
+template <int GS, bool FOLD = false>
 __global__ void unpack_stats_kernel(const uint8_t* __restrict__ packed, int64_t rows, int64_t K,
-                                    __half* __restrict__ out, uint32_t* __restrict__ stats) {
+                                    __half* __restrict__ out, uint32_t* __restrict__ stats,
+                                    const float* __restrict__ mult = nullptr, __half* __restrict__ folded = nullptr) {
   const int64_t n8 = rows * (K / 16);
   const int64_t G = K / GS;
   const int64_t loop = (n8 + 31) / 32 * 32;
@@ -138,6 +143,20 @@ __global__ void unpack_stats_kernel(const uint8_t* __restrict__ packed, int64_t 
       uint4* dst = reinterpret_cast<uint4*>(out) + 2 * i;
       dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
       dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+      if (FOLD) {
+        const int64_t r = i / (K / 16), k0 = (i % (K / 16)) * 16;
+        const float m = mult[r * G + k0 / GS];
+        uint32_t f[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const float2 v = __half22float2(*reinterpret_cast<const __half2*>(&o[q]));
+          const __half2 h = __floats2half2_rn(v.x * m, v.y * m);
+          f[q] = *reinterpret_cast<const uint32_t*>(&h);
+        }
+        uint4* fd = reinterpret_cast<uint4*>(folded) + 2 * i;
+        fd[0] = make_uint4(f[0], f[1], f[2], f[3]);
+        fd[1] = make_uint4(f[4], f[5], f[6], f[7]);
+      }
     }
     if (GS == 32) {
       l1 += __shfl_xor_sync(0xFFFFFFFFu, l1, 1);
@@ -381,30 +400,11 @@ __device__ __forceinline__ int mixed_group(const float4* __restrict__ ctm, int64
   return gx;
 }
 
-// Block-sum path operands: the fp16 "2x" operand times its integer multiplier (ma * 2^(e_g - e) for A,
-// mb * 2^(e_g - e) for B).  Exact wherever the block passes the decide test (|product| <= 65504 and at
-// most 6 significant bits); other values are never read by that path.
-__global__ void fold_rows_kernel(const __half* __restrict__ x16, int64_t rows, int64_t K, int GS,
-                                 const float* __restrict__ mult, __half* __restrict__ out) {
-  const int64_t n8 = rows * (K / 8);
-  const int64_t G = K / GS;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n8; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t r = i / (K / 8), k0 = (i % (K / 8)) * 8;
-    const float m = mult[r * G + k0 / GS];
-    const uint4 w = reinterpret_cast<const uint4*>(x16)[i];
-    uint32_t in[4] = {w.x, w.y, w.z, w.w}, o[4];
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&in[q]));
-      const __half2 h = __floats2half2_rn(f.x * m, f.y * m);
-      o[q] = *reinterpret_cast<const uint32_t*>(&h);
-    }
-    reinterpret_cast<uint4*>(out)[i] = make_uint4(o[0], o[1], o[2], o[3]);
-  }
-}
 
-// B operands: `out` every group folded (block-sum path); `out_mixed` (NVFP4) the same except the mixed
-// path's separate group of the (column tile, block), which keeps the plain "2x" values.
+// B operands, the "2x" values times their column-group multiplier (mb * 2^(e_g - e)) in fp16, exact
+// wherever a block passes the decide test: `out` every group folded (block-sum path); `out_mixed`
+// (NVFP4) the same except the mixed path's separate group of the (column tile, block), which keeps
+// the plain "2x" values.
 template <int FMT>
 __global__ void fold_cols_kernel(const __half* __restrict__ x16, int64_t N, int64_t K, int64_t tiles_n,
                                  const uint8_t* __restrict__ colrec, const float4* __restrict__ ctm,
@@ -1405,9 +1405,12 @@ static cudaError_t run_tc(const uint8_t* A, const uint8_t* B, const uint8_t* SA,
   auto grid_for = [&](int64_t n) {
     return (unsigned)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, (int64_t)sms * 16));
   };
-  unpack_stats_kernel<GS><<<grid_for(M * K / 16), 256, 0, stream>>>(A, M, K, a16, T.ast);
-  unpack_stats_kernel<GS><<<grid_for(N * K / 16), 256, 0, stream>>>(B, N, K, b16, T.bst);
+  __half* af16 = reinterpret_cast<__half*>(ws + L.af16);
+  __half* bf16 = reinterpret_cast<__half*>(ws + L.bf16);
+  // row tables first: the A unpack writes the folded A operand (row multipliers) in the same pass
   row_tables_kernel<FMT><<<grid_for(tiles_m * BM * nb), 256, 0, stream>>>(SA, M, tiles_m * BM, G, nb, sa_cols, T);
+  unpack_stats_kernel<GS, true><<<grid_for(M * K / 16), 256, 0, stream>>>(A, M, K, a16, T.ast, T.rmaq, af16);
+  unpack_stats_kernel<GS><<<grid_for(N * K / 16), 256, 0, stream>>>(B, N, K, b16, T.bst);
   col_tables_kernel<FMT><<<grid_for(Np * nb), 256, 0, stream>>>(SB, N, Np, G, nb, sb_cols, T);
   tile_stats_kernel<FMT><<<grid_for(tiles_m * G), 256, 0, stream>>>(M, BM, tiles_m, G, nb, 0, T);
   tile_stats_kernel<FMT><<<grid_for(tiles_n * G), 256, 0, stream>>>(N, BN, tiles_n, G, nb, 1, T);
@@ -1418,9 +1421,7 @@ static cudaError_t run_tc(const uint8_t* A, const uint8_t* B, const uint8_t* SA,
   uint32_t* list32 = list64 + tiles_m * tiles_n;
   uint32_t* counts = reinterpret_cast<uint32_t*>(ws + L.tile_count);
   tile_lists_kernel<<<1, 1024, 0, stream>>>(tiles_m, tiles_n, T.tile_f32, list64, list32, counts);
-  __half* af16 = reinterpret_cast<__half*>(ws + L.af16);
-  __half* bf16 = reinterpret_cast<__half*>(ws + L.bf16);
-  fold_rows_kernel<<<grid_for(M * K / 8), 256, 0, stream>>>(a16, M, K, GS, T.rmaq, af16);
+
   __half* bm16 = reinterpret_cast<__half*>(ws + L.bm16);
   fold_cols_kernel<FMT><<<grid_for(N * K / 8), 256, 0, stream>>>(b16, N, K, tiles_n, T.colrec, T.ctm, bf16, bm16);
   e = cudaGetLastError();
