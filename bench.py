@@ -481,6 +481,7 @@ def main() -> int:
         dist.barrier()
     ms_local = t0.elapsed_time(t1)
     gemm_ms = sum(s.elapsed_time(e) for s, e in gemm_ev) / args.steps
+    finite_frac = float(torch.isfinite(out).float().mean())
 
     # ---- end to end: pinned host inputs -> device -> quant + emul -> host output, every step.  The
     # copies run on their own streams with two device input buffers, so step i's host->device copy
@@ -578,6 +579,11 @@ def main() -> int:
                          "cuda_core": {"what": "stage-4 chain: DADD + DFMA per output and K block, FP64 pipe",
                                        "fp64_ops": fp64_ops, "peak_ops_per_s": 64.0 * n_sm * mhz * 1e6,
                                        "floor_ms": fp64_floor_ms, "frac": fp64_floor_ms / gemm_max}},
+            # emul_fn returns fp16 like the reference emulator (nvfp_emulation.cpp:155); at this data
+            # |C| is about 5e5 (82 outlier channels x 100 x 100), above fp16's 65504, so the returned
+            # values saturate to inf there exactly as the reference's do -- the f32 accumulation before
+            # that final conversion is computed in full
+            "output": {"dtype": str(out.dtype).replace("torch.", ""), "finite_frac": finite_frac},
             "gpu_launches": None if launches_per_step is None else launches_per_step * args.steps,
             "clocks": clk.summary(),
         }

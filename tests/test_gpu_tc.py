@@ -77,7 +77,8 @@ def test_tc_vs_oracle_and_simt(case):
 
 def test_tc_8192_sampled_against_oracle():
     """The benchmark shape (8192^3 NVFP4, |N(0,1)| + outlier columns, quantised by libemugen): full
-    tensor-core launch, 64 sampled outputs re-derived by the oracle on row / column slices."""
+    tensor-core launch, 64 sampled outputs re-derived by the oracle on row / column slices, in fp16 (the
+    emulator's output, saturated at this data) and in the f32 output mode (the accumulator)."""
     from emugen_b200 import nvfp4_global_scales, quant_nvfp4
     from tests.golden.make_golden import pad, swizzle
 
@@ -95,6 +96,8 @@ def test_tc_8192_sampled_against_oracle():
     a, b, sfa, sfb = qa.cpu().numpy(), qb.cpu().numpy(), sfa.cpu().numpy(), sfb.cpu().numpy()
     al = float(alpha.item())
     got = _bits(_run(a, b, sfa, sfb, "nvfp", 0, 0, al, 0, "tc"))
+    # f32 output mode: the accumulator itself (|C| ~ 5e5 here, so the fp16 output is +inf everywhere)
+    got32 = _run(a, b, sfa, sfb, "nvfp", 0, 0, al, 2, "tc").cpu().numpy()
     rng = np.random.default_rng(5)
     rows = rng.choice(M, 8, replace=False)
     cs = rng.choice(N, 8, replace=False)
@@ -110,6 +113,11 @@ def test_tc_8192_sampled_against_oracle():
     ref = oracle.emul_gemm(a[rows], b[cs], lin(sfa, rows), lin(sfb, cs), scale_fmt=0, group_size=16, w_reduce=4,
                            alpha=al, out_mode=0)
     assert nan_equal_mismatches(got[np.ix_(rows, cs)], ref, "float16") == 0
+    ref32 = oracle.emul_gemm(a[rows], b[cs], lin(sfa, rows), lin(sfb, cs), scale_fmt=0, group_size=16, w_reduce=4,
+                             alpha=al, out_mode=2)
+    g32 = np.ascontiguousarray(got32[np.ix_(rows, cs)])
+    assert np.isfinite(g32).all() and np.abs(g32).min() > 65504
+    assert (g32.view(np.uint32) != np.ascontiguousarray(ref32).view(np.uint32)).sum() == 0
 
 
 OUTLIER_CASES = [("nvfp", True, 0, 0, 0, 100.0), ("nvfp", False, 1, 1, 1, 100.0), ("nvfp", True, 1, 0, 2, 1000.0),
