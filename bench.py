@@ -90,8 +90,8 @@ def peaks():
 
 
 class ClockSampler:
-    """SM clock, power and clock-event reasons of this process's GPU, sampled every 20 ms through NVML
-    (read-only queries) while the timed region runs; nvidia-smi at 100 ms when NVML is unavailable."""
+    """SM clock and clock-event reasons of this process's GPU, sampled every 5 ms through NVML
+    (read-only queries) while a timed region runs; nvidia-smi at 100 ms when NVML is unavailable."""
 
     REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
                0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
@@ -129,7 +129,7 @@ class ClockSampler:
                                              nv.nvmlDeviceGetCurrentClocksEventReasons(h)))
                     except Exception:
                         pass
-                    self._stop.wait(0.02)
+                    self._stop.wait(0.005)
 
             self._thread = threading.Thread(target=run, daemon=True)
             self._thread.start()
@@ -523,13 +523,15 @@ def main() -> int:
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    e0.record(stream)
-    s_in.wait_stream(stream)
-    s_out.wait_stream(stream)
-    e2e_steps(args.steps)
-    e1.record(stream)
-    torch.cuda.synchronize()
+    with ClockSampler(local) as clk_e2e:
+        e0.record(stream)
+        s_in.wait_stream(stream)
+        s_out.wait_stream(stream)
+        e2e_steps(args.steps)
+        e1.record(stream)
+        torch.cuda.synchronize()
     e2e_local = e0.elapsed_time(e1)
+    clk.samples += clk_e2e.samples     # the clock record covers both timed regions
 
     times = torch.tensor([ms_local, e2e_local, gemm_ms], dtype=torch.float64, device=dev)
     if world > 1:
