@@ -26,6 +26,14 @@ CASES = [
     ("mxfp", "raw_scales_full", 16, 64, 256, 2, 0, 1, 2),
     ("mxfp", "subnormal_acc", 33, 80, 512, 1, 1, 1, 0),
     ("mxfp", "flt_max", 7, 70, 128, 2, 0, 0, 2),
+    # one row of A (its own kernel, 4096-element K windows): several windows and a partial last one,
+    # windows of 64 blocks (w_reduce 1, 2, 4) and of 16 blocks (w_reduce 16), a partial 32-column tile
+    ("nvfp", "normal", 1, 170, 9216, 4, 0, 0, 0),
+    ("nvfp", "outliers", 1, 70, 4160, 1, 1, 1, 2),
+    ("nvfp", "cancel", 1, 64, 5120, 16, 0, 1, 0),
+    ("nvfp", "raw_nan_scales", 1, 96, 4608, 4, 1, 1, 1),
+    ("mxfp", "student_t", 1, 100, 8256, 2, 1, 0, 1),
+    ("mxfp", "subnormal_acc", 1, 40, 6144, 1, 0, 0, 2),
 ]
 
 
