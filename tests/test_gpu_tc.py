@@ -120,6 +120,43 @@ def test_tc_8192_sampled_against_oracle():
     assert (g32.view(np.uint32) != np.ascontiguousarray(ref32).view(np.uint32)).sum() == 0
 
 
+def test_tc_mxfp4_8192_sampled_against_oracle():
+    """MXFP4 at 8192^3 (bf16 ~N(0,1) inputs, quantised by libemugen): the f32 block-sum launch at full
+    size.  64 sampled outputs re-derived by the oracle on row / column slices, in
+    the f32 output mode (the accumulator) and in bf16 (fp16 then bf16, the reference's output path)."""
+    from emugen_b200 import quant_mxfp4
+    from tests.golden.make_golden import pad, swizzle
+
+    g = torch.Generator().manual_seed(11)
+    M = N = K = 8192
+    xa = torch.randn(M, K, generator=g).bfloat16().cuda()
+    xb = torch.randn(N, K, generator=g).bfloat16().cuda()
+    qa, sfa = quant_mxfp4(xa)
+    qb, sfb = quant_mxfp4(xb)
+    a, b, sfa, sfb = qa.cpu().numpy(), qb.cpu().numpy(), sfa.cpu().numpy(), sfb.cpu().numpy()
+    got32 = _run(a, b, sfa, sfb, "mxfp", 0, 0, None, 2, "tc").cpu().numpy()
+    got16 = _bits(_run(a, b, sfa, sfb, "mxfp", 0, 0, None, 1, "tc"))
+    rng = np.random.default_rng(6)
+    rows = rng.choice(M, 8, replace=False)
+    cs = rng.choice(N, 8, replace=False)
+    G = K // 32
+
+    def lin(sf, idx):
+        flat = sf.reshape(-1)
+        out = np.empty((len(idx), G), dtype=np.uint8)
+        for i, r in enumerate(idx):
+            out[i] = [flat[oracle.swizzle_offset(int(r), c, pad(G, 4))] for c in range(G)]
+        return swizzle(out, 128, pad(G, 4))
+
+    la, lb = lin(sfa, rows), lin(sfb, cs)
+    ref32 = oracle.emul_gemm(a[rows], b[cs], la, lb, scale_fmt=1, group_size=32, w_reduce=2, out_mode=2)
+    g32 = np.ascontiguousarray(got32[np.ix_(rows, cs)])
+    assert np.isfinite(g32).all()
+    assert (g32.view(np.uint32) != np.ascontiguousarray(ref32).view(np.uint32)).sum() == 0
+    ref16 = oracle.emul_gemm(a[rows], b[cs], la, lb, scale_fmt=1, group_size=32, w_reduce=2, out_mode=1)
+    assert nan_equal_mismatches(got16[np.ix_(rows, cs)], ref16, "bfloat16") == 0
+
+
 OUTLIER_CASES = [("nvfp", True, 0, 0, 0, 100.0), ("nvfp", False, 1, 1, 1, 100.0), ("nvfp", True, 1, 0, 2, 1000.0),
                  ("nvfp", False, 0, 1, 0, 30.0), ("mxfp", True, 0, 0, 1, 1000.0), ("mxfp", False, 1, 1, 0, 1e4),
                  # shrunken channels: finer quanta than the rest, so the exactness bound of the f32
