@@ -106,7 +106,7 @@ static emu_status validate_gemm(int64_t M, int64_t N, int64_t K, int64_t scale_a
     return fail(EMU_ERR_INVALID_ARGUMENT, "rounding must be EMU_RZ (0) or EMU_RNE (1)");
   if (p.out_mode < EMU_OUT_F16 || p.out_mode > EMU_OUT_F32)
     return fail(EMU_ERR_INVALID_ARGUMENT, "unknown out_mode %d", p.out_mode);
-  if ((N + 63) / 64 > 65535) return fail(EMU_ERR_UNSUPPORTED, "N too large for this build (max 4194240)");
+  if ((N + 63) / 64 > 65535) return fail(EMU_ERR_UNSUPPORTED, "N too large for the tensor-core tile index (max 4194240)");
   return EMU_OK;
 }
 

@@ -47,7 +47,7 @@ enum {
   EMU_ERR_GROUP_SIZE = 5,         /* "only MXFP4 group_size=32 is supported" (and NVFP4: 16)     */
   EMU_ERR_SCALE_SHAPE = 6,        /* "swizzled scale shape must be divisible by 128 and 4"        */
   EMU_ERR_SCALE_TOO_SMALL = 7,    /* scale buffer has fewer rows / columns than M,N / K/group     */
-  EMU_ERR_UNSUPPORTED = 8,        /* a size beyond what this build supports (message says which)  */
+  EMU_ERR_UNSUPPORTED = 8,        /* a size beyond what this library supports (message says which) */
   EMU_ERR_CUDA = 9                /* a CUDA runtime error (message carries cudaGetErrorString)    */
 };
 

@@ -1,6 +1,6 @@
 /*
  * CPU oracle for the emulated NVFP4 / MXFP4 scaled GEMM.  TEST INFRASTRUCTURE ONLY:
- * tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg call it as the checker.
+ * tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg call it, to check results.
  * The product path (emugen_b200, libemugen.so) never links, loads or calls this file.
  *
  * It restates, in plain C, the arithmetic of the reference emulators:

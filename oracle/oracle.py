@@ -1,7 +1,7 @@
 """ctypes wrapper around ``_build/liboracle.so`` (the C restatement in ``emul_oracle.c``).
 
 TEST INFRASTRUCTURE ONLY: imported by tests/, ``__graft_entry__.smoke()`` and the CPU-baseline leg
-of ``bench.py`` as the checker; the product package ``emugen_b200`` never imports it.
+of ``bench.py`` to check results; the product package ``emugen_b200`` never imports it.
 """
 from __future__ import annotations
 

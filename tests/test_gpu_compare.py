@@ -11,7 +11,7 @@ pytestmark = pytest.mark.gpu
 
 
 def _ref_compare(real, model, sample_count=5):
-    """gemm_compare/runner.py:20-55 restated with torch ops (the checker)."""
+    """gemm_compare/runner.py:20-55 restated with torch ops (the comparison the tests check against)."""
     diff = (real.float() - model.float()).abs()
     diff[real == model] = 0.0
     diff[real.isnan() & model.isnan()] = 0.0
