@@ -149,13 +149,33 @@ __device__ __forceinline__ unsigned half_bits_to_float_bits(unsigned h) {
   else return h << 16;
 }
 
+// amax of A (blockIdx.y == 0) and B (blockIdx.y == 1) in one launch, as the bits of a non-negative
+// float (atomicMax on unsigned orders them like the values): 16-bit magnitudes compared two at a time,
+// four 16-byte loads in flight per thread, the unaligned remainder element by element.
 template <typename T>
-__global__ void amax_bits_kernel(const T* __restrict__ x, int64_t n, unsigned* __restrict__ out) {
+__global__ void amax_bits_kernel(const T* __restrict__ xa, int64_t na, const T* __restrict__ xb, int64_t nb,
+                                 unsigned* __restrict__ out_a, unsigned* __restrict__ out_b) {
+  const T* x = blockIdx.y ? xb : xa;
+  const int64_t n = blockIdx.y ? nb : na;
+  unsigned* out = blockIdx.y ? out_b : out_a;
   unsigned m2 = 0;   // two 16-bit magnitude maxima
   const int64_t n8 = (reinterpret_cast<uintptr_t>(x) & 15) == 0 ? n / 8 : 0;
   const uint4* x8 = reinterpret_cast<const uint4*>(x);
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n8; i += stride) {
+  int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  for (; i + 3 * stride < n8; i += 4 * stride) {
+    uint4 w[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) w[u] = __ldg(x8 + i + u * stride);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      m2 = __vmaxu2(m2, w[u].x & 0x7FFF7FFFu);
+      m2 = __vmaxu2(m2, w[u].y & 0x7FFF7FFFu);
+      m2 = __vmaxu2(m2, w[u].z & 0x7FFF7FFFu);
+      m2 = __vmaxu2(m2, w[u].w & 0x7FFF7FFFu);
+    }
+  }
+  for (; i < n8; i += stride) {
     const uint4 w = __ldg(x8 + i);
     m2 = __vmaxu2(m2, w.x & 0x7FFF7FFFu);
     m2 = __vmaxu2(m2, w.y & 0x7FFF7FFFu);
@@ -163,8 +183,8 @@ __global__ void amax_bits_kernel(const T* __restrict__ x, int64_t n, unsigned* _
     m2 = __vmaxu2(m2, w.w & 0x7FFF7FFFu);
   }
   const unsigned short* xs = reinterpret_cast<const unsigned short*>(x);
-  for (int64_t i = n8 * 8 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += stride)
-    m2 = __vmaxu2(m2, (unsigned)xs[i] & 0x7FFFu);
+  for (int64_t j = n8 * 8 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; j < n; j += stride)
+    m2 = __vmaxu2(m2, (unsigned)xs[j] & 0x7FFFu);
   unsigned m = half_bits_to_float_bits<T>(max(m2 & 0xFFFFu, m2 >> 16));
   for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
   if ((threadIdx.x & 31) == 0) atomicMax(out, m);
@@ -216,13 +236,21 @@ cudaError_t launch_global_scales(const void* a, int64_t a_numel, const void* b, 
   cudaError_t err = cudaMemsetAsync(gs_a, 0, sizeof(float), stream);
   if (err == cudaSuccess) err = cudaMemsetAsync(gs_b, 0, sizeof(float), stream);
   if (err != cudaSuccess) return err;
-  auto grid_for = [](int64_t n) { return (unsigned)std::min<int64_t>(std::max<int64_t>((n + 255) / 256, 1), 148 * 16); };
+  // one wave: 4 CTAs of 256 threads per SM and tensor, each thread four 16-byte loads per step
+  const int64_t n_max = std::max(a_numel, b_numel);
+  int sms = 148;
+  {
+    int dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  }
+  const dim3 grid((unsigned)std::min<int64_t>(std::max<int64_t>((n_max / 8 + 1023) / 1024, 1), (int64_t)sms * 4), 2);
   if (dtype == EMU_DTYPE_F16) {
-    amax_bits_kernel<__half><<<grid_for(a_numel), 256, 0, stream>>>(static_cast<const __half*>(a), a_numel, reinterpret_cast<unsigned*>(gs_a));
-    amax_bits_kernel<__half><<<grid_for(b_numel), 256, 0, stream>>>(static_cast<const __half*>(b), b_numel, reinterpret_cast<unsigned*>(gs_b));
+    amax_bits_kernel<__half><<<grid, 256, 0, stream>>>(static_cast<const __half*>(a), a_numel, static_cast<const __half*>(b),
+                                                      b_numel, reinterpret_cast<unsigned*>(gs_a), reinterpret_cast<unsigned*>(gs_b));
   } else {
-    amax_bits_kernel<__nv_bfloat16><<<grid_for(a_numel), 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(a), a_numel, reinterpret_cast<unsigned*>(gs_a));
-    amax_bits_kernel<__nv_bfloat16><<<grid_for(b_numel), 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(b), b_numel, reinterpret_cast<unsigned*>(gs_b));
+    amax_bits_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(
+        static_cast<const __nv_bfloat16*>(a), a_numel, static_cast<const __nv_bfloat16*>(b), b_numel,
+        reinterpret_cast<unsigned*>(gs_a), reinterpret_cast<unsigned*>(gs_b));
   }
   global_scales_finalize<<<1, 1, 0, stream>>>(gs_a, gs_b, alpha);
   return cudaGetLastError();
