@@ -25,8 +25,10 @@ EMU_DTYPE_F16, EMU_DTYPE_BF16, EMU_DTYPE_F32 = 0, 1, 2
 ABI_VERSION = 1
 
 SYMBOLS = ("emu_abi_version", "emu_last_error", "emu_status_string", "emu_gemm", "emu_gemm_workspace_size", "emu_gemm_tc_workspace_size",
-           "emu_gemm_ws", "emu_gemm_static", "emu_nvfp4_global_scales", "emu_quant_nvfp4", "emu_quant_mxfp4",
-           "emu_gemm_model", "emu_gemm_compare", "emu_compare", "emu_dequant_fp4")
+           "emu_gemm_ws", "emu_gemm_tc_path_offset", "emu_gemm_static", "emu_nvfp4_global_scales", "emu_nvfp4_amax",
+           "emu_nvfp4_scales_from_amax", "emu_quant_nvfp4", "emu_quant_mxfp4",
+           "emu_gemm_model", "emu_gemm_compare", "emu_compare", "emu_dequant_fp4", "emu_device_status",
+           "emu_set_wait_limit", "emu_test_hold_first_ready")
 STATIC_SCRATCH_BYTES = 64 << 20   # EMU_STATIC_SCRATCH_BYTES
 
 
@@ -84,6 +86,8 @@ def load() -> ctypes.CDLL:
         L.emu_gemm_workspace_size.argtypes = [i64, i64, i64, ctypes.POINTER(EmuGemmParams)]
         L.emu_gemm_tc_workspace_size.restype = ctypes.c_size_t
         L.emu_gemm_tc_workspace_size.argtypes = [i64, i64, i64, ctypes.POINTER(EmuGemmParams)]
+        L.emu_gemm_tc_path_offset.restype = ctypes.c_size_t
+        L.emu_gemm_tc_path_offset.argtypes = [i64, i64, i64, ctypes.POINTER(EmuGemmParams)]
         L.emu_gemm_ws.restype = i32
         L.emu_gemm_ws.argtypes = [vp, vp, vp, vp, i64, i64, i64, i64, i64, i64, i64, vp,
                                   ctypes.POINTER(EmuGemmParams), vp, vp, ctypes.c_size_t, vp]
@@ -92,6 +96,10 @@ def load() -> ctypes.CDLL:
                                       ctypes.POINTER(EmuGemmParams), vp, vp]
         L.emu_nvfp4_global_scales.restype = i32
         L.emu_nvfp4_global_scales.argtypes = [vp, i64, vp, i64, i32, vp, vp, vp, vp]
+        L.emu_nvfp4_amax.restype = i32
+        L.emu_nvfp4_amax.argtypes = [vp, i64, vp, i64, i32, vp, vp, vp]
+        L.emu_nvfp4_scales_from_amax.restype = i32
+        L.emu_nvfp4_scales_from_amax.argtypes = [vp, vp, vp, vp, vp, vp]
         L.emu_quant_nvfp4.restype = i32
         L.emu_quant_nvfp4.argtypes = [vp, i32, i64, i64, vp, vp, vp, vp]
         L.emu_quant_mxfp4.restype = i32
@@ -106,6 +114,12 @@ def load() -> ctypes.CDLL:
         L.emu_compare.argtypes = [vp, vp, i32, i64, vp, vp]
         L.emu_dequant_fp4.restype = i32
         L.emu_dequant_fp4.argtypes = [vp, vp, i64, i64, i64, i32, vp, vp, vp]
+        L.emu_device_status.restype = i32
+        L.emu_device_status.argtypes = [vp]
+        L.emu_set_wait_limit.restype = i64
+        L.emu_set_wait_limit.argtypes = [i64]
+        L.emu_test_hold_first_ready.restype = i32
+        L.emu_test_hold_first_ready.argtypes = [i32]
         v = L.emu_abi_version()
         if v != ABI_VERSION:
             raise ImportError(f"libemugen ABI version {v}, expected {ABI_VERSION}: rebuild it")
@@ -117,6 +131,27 @@ def _check(status: int) -> None:
     if status != EMU_OK:
         L = load()
         raise EmuError(status, L.emu_last_error().decode() or L.emu_status_string(status).decode())
+
+
+EMU_ERR_TIMEOUT = 10
+
+
+def device_status(device: torch.device | int | None = None) -> None:
+    """Synchronise the device's current stream and raise EmuError if a tensor-core pipeline wait ran
+    out since the last check (emu_device_status); the outputs of those calls are undefined."""
+    L = load()
+    if device is None:
+        dev = torch.device("cuda", torch.cuda.current_device())
+    else:
+        dev = torch.device("cuda", device) if isinstance(device, int) else torch.device(device)
+    with torch.cuda.device(dev):
+        _check(L.emu_device_status(_stream(dev)))
+
+
+def set_wait_limit(cycles: int) -> int:
+    """Bound (SM cycles) of each pipeline wait in later tensor-core launches; <= 0 restores the
+    default (2^31).  Returns the previous bound."""
+    return int(load().emu_set_wait_limit(int(cycles)))
 
 
 def _device_for(*tensors: torch.Tensor) -> torch.device:
@@ -188,7 +223,10 @@ def gemm(a_fp4: torch.Tensor, b_fp4: torch.Tensor, scale_a: torch.Tensor, scale_
                            None if al is None else al.data_ptr(), ctypes.byref(params), out.data_ptr(),
                            ws_ptr, ws_bytes, _stream(dev))
     _check(st)
-    return out.cpu() if on_cpu else out
+    if on_cpu:   # the copy back synchronises anyway: report a failed device pipeline here
+        device_status(dev)
+        return out.cpu()
+    return out
 
 
 def _dtype_code(x: torch.Tensor) -> int:
@@ -215,6 +253,36 @@ def nvfp4_global_scales(a: torch.Tensor, b: torch.Tensor):
                                        gsa.data_ptr(), gsb.data_ptr(), al.data_ptr(), _stream(dev))
     _check(st)
     return gsa, gsb, al
+
+
+def nvfp4_amax(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """max|a| and max|b| as an int32 [2] device tensor of f32 bit patterns (emu_nvfp4_amax): shards of
+    an operand combine with an integer MAX (torch.distributed all_reduce MAX)."""
+    L = load()
+    dev = _device_for(a, b)
+    if a.dtype != b.dtype:
+        raise RuntimeError("a and b must have the same dtype")
+    a_, b_ = a.to(dev).contiguous(), b.to(dev).contiguous()
+    words = torch.empty(2, dtype=torch.int32, device=dev)
+    with torch.cuda.device(dev):
+        st = L.emu_nvfp4_amax(a_.data_ptr(), a_.numel(), b_.data_ptr(), b_.numel(), _dtype_code(a_),
+                              words.data_ptr(), words.data_ptr() + 4, _stream(dev))
+    _check(st)
+    return words
+
+
+def nvfp4_scales_from_amax(words: torch.Tensor):
+    """(gs_a, gs_b, alpha) device float32[1] tensors from nvfp4_amax words (emu_nvfp4_scales_from_amax)."""
+    L = load()
+    if words.dtype != torch.int32 or words.numel() != 2 or not words.is_cuda:
+        raise RuntimeError("words must be the int32 [2] CUDA tensor nvfp4_amax returns")
+    w = words.contiguous()
+    out = torch.empty(3, dtype=torch.float32, device=w.device)
+    with torch.cuda.device(w.device):
+        st = L.emu_nvfp4_scales_from_amax(w.data_ptr(), w.data_ptr() + 4, out.data_ptr(), out.data_ptr() + 4,
+                                          out.data_ptr() + 8, _stream(w.device))
+    _check(st)
+    return out[0:1], out[1:2], out[2:3]
 
 
 def _quant(x: torch.Tensor, sf_vec: int, gs: torch.Tensor | None):
@@ -273,6 +341,7 @@ def compare_stats(ref: torch.Tensor, out: torch.Tensor) -> dict:
     with torch.cuda.device(dev):
         status = L.emu_compare(r.data_ptr(), o.data_ptr(), _cmp_dtype(r), r.numel(), st.data_ptr(), _stream(dev))
     _check(status)
+    device_status(dev)   # reading the statistics synchronises anyway
     host = EmuCompareStats.from_buffer_copy(bytes(st.cpu().numpy()))
     return {k: getattr(host, k) for k, _ in EmuCompareStats._fields_}
 
@@ -334,6 +403,7 @@ def gemm_compare(a_fp4: torch.Tensor, b_fp4: torch.Tensor, scale_a: torch.Tensor
                                     None if out is None else out.data_ptr(), st.data_ptr(), ws_ptr, ws_bytes,
                                     _stream(dev))
     _check(status)
+    device_status(dev)   # reading the statistics synchronises anyway
     host = EmuCompareStats.from_buffer_copy(bytes(st.cpu().numpy()))
     return {k: getattr(host, k) for k, _ in EmuCompareStats._fields_}, out
 

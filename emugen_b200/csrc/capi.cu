@@ -61,6 +61,7 @@ const char* emu_status_string(emu_status s) {
     case EMU_ERR_SCALE_TOO_SMALL: return "EMU_ERR_SCALE_TOO_SMALL";
     case EMU_ERR_UNSUPPORTED: return "EMU_ERR_UNSUPPORTED";
     case EMU_ERR_CUDA: return "EMU_ERR_CUDA";
+    case EMU_ERR_TIMEOUT: return "EMU_ERR_TIMEOUT";
     default: return "EMU_ERR_UNKNOWN";
   }
 }
@@ -137,10 +138,14 @@ size_t emu_gemm_tc_workspace_size(int64_t M, int64_t N, int64_t K, const emu_gem
   return workspace_for(M, N, K, params, false);
 }
 
-emu_status emu_gemm_ws(const uint8_t* a_fp4, const uint8_t* b_fp4, const uint8_t* scale_a, const uint8_t* scale_b,
-                       int64_t M, int64_t N, int64_t K, int64_t scale_a_rows, int64_t scale_a_cols,
-                       int64_t scale_b_rows, int64_t scale_b_cols, const float* alpha, const emu_gemm_params* params,
-                       void* out, void* workspace, size_t workspace_bytes, void* stream) {
+}  // extern "C"
+
+// Every check emu_gemm_ws makes before it looks at the workspace: sizes, parameters, scale shapes
+// (validate_gemm), then the tensor pointers.  Sets emu_last_error() on failure.
+emu_status emu::check_gemm_call(const uint8_t* a_fp4, const uint8_t* b_fp4, const uint8_t* scale_a,
+                                const uint8_t* scale_b, int64_t M, int64_t N, int64_t K, int64_t scale_a_rows,
+                                int64_t scale_a_cols, int64_t scale_b_rows, int64_t scale_b_cols,
+                                const emu_gemm_params* params, const void* out) {
   emu_status st = validate_gemm(M, N, K, scale_a_rows, scale_a_cols, scale_b_rows, scale_b_cols, params);
   if (st != EMU_OK) return st;
   if (M == 0 || N == 0) return ok();
@@ -148,6 +153,24 @@ emu_status emu_gemm_ws(const uint8_t* a_fp4, const uint8_t* b_fp4, const uint8_t
     return fail(EMU_ERR_INVALID_ARGUMENT, "tensor pointers must not be NULL");
   if (!aligned(a_fp4, 16) || !aligned(b_fp4, 16))
     return fail(EMU_ERR_INVALID_ARGUMENT, "a_fp4 / b_fp4 must be 16-byte aligned");
+  return ok();
+}
+
+extern "C" {
+
+size_t emu_gemm_tc_path_offset(int64_t M, int64_t N, int64_t K, const emu_gemm_params* params) {
+  if (workspace_for(M, N, K, params, false) == 0) return (size_t)-1;
+  return emu::gemm_tc_path_offset(params->format, M, N, K);
+}
+
+emu_status emu_gemm_ws(const uint8_t* a_fp4, const uint8_t* b_fp4, const uint8_t* scale_a, const uint8_t* scale_b,
+                       int64_t M, int64_t N, int64_t K, int64_t scale_a_rows, int64_t scale_a_cols,
+                       int64_t scale_b_rows, int64_t scale_b_cols, const float* alpha, const emu_gemm_params* params,
+                       void* out, void* workspace, size_t workspace_bytes, void* stream) {
+  emu_status st = emu::check_gemm_call(a_fp4, b_fp4, scale_a, scale_b, M, N, K, scale_a_rows, scale_a_cols,
+                                       scale_b_rows, scale_b_cols, params, out);
+  if (st != EMU_OK) return st;
+  if (M == 0 || N == 0) return ok();
   const emu_gemm_params p = *params;
   emu::GemmArgs args{p.format, p.w_reduce, p.stage3_rounding, p.stage4_rounding, p.out_mode};
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -187,6 +210,24 @@ emu_status emu_nvfp4_global_scales(const void* a, int64_t a_numel, const void* b
   cudaError_t e = emu::launch_global_scales(a, a_numel, b, b_numel, dtype, gs_a, gs_b, alpha,
                                             static_cast<cudaStream_t>(stream));
   return cuda_status(e, "emu_nvfp4_global_scales launch");
+}
+
+emu_status emu_nvfp4_amax(const void* a, int64_t a_numel, const void* b, int64_t b_numel, int32_t dtype,
+                          uint32_t* amax_a, uint32_t* amax_b, void* stream) {
+  if (!a || !b || !amax_a || !amax_b) return fail(EMU_ERR_INVALID_ARGUMENT, "pointers must not be NULL");
+  if (a_numel < 0 || b_numel < 0) return fail(EMU_ERR_INVALID_ARGUMENT, "negative size");
+  if (dtype != EMU_DTYPE_F16 && dtype != EMU_DTYPE_BF16)
+    return fail(EMU_ERR_INVALID_ARGUMENT, "dtype must be EMU_DTYPE_F16 or EMU_DTYPE_BF16");
+  if (!aligned(amax_a, 4) || !aligned(amax_b, 4)) return fail(EMU_ERR_INVALID_ARGUMENT, "amax words must be 4-byte aligned");
+  return cuda_status(emu::launch_amax(a, a_numel, b, b_numel, dtype, amax_a, amax_b, static_cast<cudaStream_t>(stream)),
+                     "emu_nvfp4_amax launch");
+}
+
+emu_status emu_nvfp4_scales_from_amax(const uint32_t* amax_a, const uint32_t* amax_b, float* gs_a, float* gs_b,
+                                      float* alpha, void* stream) {
+  if (!amax_a || !amax_b || !gs_a || !gs_b) return fail(EMU_ERR_INVALID_ARGUMENT, "pointers must not be NULL");
+  return cuda_status(emu::launch_scales_from_amax(amax_a, amax_b, gs_a, gs_b, alpha, static_cast<cudaStream_t>(stream)),
+                     "emu_nvfp4_scales_from_amax launch");
 }
 
 static emu_status quant_common(int sf_vec, const void* x, int32_t dtype, int64_t M, int64_t K,
@@ -299,6 +340,28 @@ emu_status emu_gemm_compare(const uint8_t* a_fp4, const uint8_t* b_fp4, const ui
                                         args, out, s);
   if (e == cudaSuccess) e = emu::launch_compare(ref, out, cmp_dtype, M * N, stats, s);
   return cuda_status(e, "emu_gemm_compare launch");
+}
+
+int64_t emu_set_wait_limit(int64_t cycles) { return emu::set_wait_limit(cycles); }
+
+emu_status emu_test_hold_first_ready(int32_t enable) {
+  emu::set_hold_first_ready(enable);
+  return ok();
+}
+
+emu_status emu_device_status(void* stream) {
+  cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_status(e, "emu_device_status: stream");
+  int code = 0;
+  e = emu::take_wait_error(&code);
+  if (e != cudaSuccess) return cuda_status(e, "emu_device_status: error word");
+  if (code == 0) return ok();
+  static const char* const kSite[] = {"", "producer stage slot", "producer record slot", "MMA accumulator set",
+                                      "MMA stage data", "epilogue accumulator", "epilogue records",
+                                      "producer drain", "record drain", "MMA drain"};
+  return fail(EMU_ERR_TIMEOUT,
+              "a tensor-core pipeline wait ran out (code %d: %s); outputs of the calls on this device since the "
+              "last emu_device_status are undefined", code, code > 0 && code < 10 ? kSite[code] : "unknown");
 }
 
 emu_status emu_dequant_fp4(const uint8_t* q, const uint8_t* sf, int64_t rows, int64_t K, int64_t sf_cols,

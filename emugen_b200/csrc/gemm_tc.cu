@@ -53,6 +53,7 @@
 #include <stdlib.h>
 
 #include <algorithm>
+#include <atomic>
 #include <type_traits>
 
 #include "common.cuh"
@@ -617,8 +618,27 @@ struct Params {
   const float* alpha;
   void* out;
   int* err;
+  long long wait_limit;          // cycles a pipeline wait may take before the kernel gives up
+  int hold_first_ready;          // test hook: the MMA warp withholds block 0's accumulator-ready signal
   int r3, r4, out_mode;
 };
+
+// Per device: the code of the first pipeline wait that ran out since the last emu_device_status
+// (0 = none).  Codes: 1 producer stage slot, 2 producer record slot, 3 MMA accumulator set, 4 MMA
+// stage data, 5 epilogue accumulator, 6 epilogue records, 7-9 drains at exit.
+__device__ int g_wait_error;
+constexpr long long DRAIN_LIMIT = 1ll << 31;   // waits for copies / MMAs already in flight
+
+// A pipeline wait bounded by the launch's limit (drains by DRAIN_LIMIT, so that every copy and MMA
+// the CTA issued has landed before it exits); on expiry records `code` in the workspace's error
+// word and the device's sticky word (first error wins in each) and returns false.
+__device__ __forceinline__ bool wait_or_record(uint64_t* bar, uint32_t parity, const Params& p, int code,
+                                               bool drain = false) {
+  if (ptx::mbar_wait(bar, parity, drain ? DRAIN_LIMIT : p.wait_limit)) return true;
+  atomicCAS(p.err, 0, code);
+  atomicCAS(&g_wait_error, 0, code);
+  return false;
+}
 
 __device__ __forceinline__ void tile_coords(int64_t t, int64_t tiles_m, int64_t tiles_n, int64_t& tm, int64_t& tn) {
   const int64_t per_band = (int64_t)GROUP_M * tiles_n;
@@ -852,7 +872,7 @@ emul_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
           tn = tid & 0xFFFFu;
           for (int64_t kb = 0; kb < p.nb && ok; ++kb, ++it) {
             const int s = (int)(it % NSTAGE);
-            ok = ptx::mbar_wait(&empty[s], (uint32_t)((it / NSTAGE) & 1) ^ 1u, p.err, 1);
+            ok = wait_or_record(&empty[s], (uint32_t)((it / NSTAGE) & 1) ^ 1u, p, 1);
             if (!ok) break;
             uint8_t* sa = stage_base + s * STAGE_BYTES;
             // block-sum blocks read both folded operands, mixed blocks the folded A and the mixed B,
@@ -867,7 +887,7 @@ emul_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
             ptx::tma_load_2d(sa + A_BYTES, path == PATH_SUM ? &tmBF : path == PATH_MIXED ? &tmBM : &tmB, &full[s],
                              (int)(kb * BK), (int)(tn * BN));
             const int q = (int)(it % NCR);
-            ok = ptx::mbar_wait(&cr_empty[q], (uint32_t)((it / NCR) & 1) ^ 1u, p.err, 2);
+            ok = wait_or_record(&cr_empty[q], (uint32_t)((it / NCR) & 1) ^ 1u, p, 2);
             if (!ok) break;
             // column record bytes each path reads: block-sum the column factors, integer also the
             // multipliers and bias constants, f64 the f64 scales as well
@@ -883,9 +903,9 @@ emul_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
         }
         // drain: every issued copy must have landed before the CTA may exit (bounded waits)
         for (int64_t j = (it > NSTAGE ? it - NSTAGE : 0); j < it; ++j)
-          ptx::mbar_wait(&full[j % NSTAGE], (uint32_t)((j / NSTAGE) & 1), p.err, 7);
+          wait_or_record(&full[j % NSTAGE], (uint32_t)((j / NSTAGE) & 1), p, 7, true);
         for (int64_t j = (it > NCR ? it - NCR : 0); j < it; ++j)
-          ptx::mbar_wait(&cr_full[j % NCR], (uint32_t)((j / NCR) & 1), p.err, 8);
+          wait_or_record(&cr_full[j % NCR], (uint32_t)((j / NCR) & 1), p, 8, true);
       }
     } else if (warp == 1) {
       // ---------------------------------------------------------------- MMA issuer
@@ -898,9 +918,9 @@ emul_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
           for (int64_t kb = 0; kb < p.nb && ok; ++kb, ++it) {
             const int s = (int)(it % NSTAGE);
             const int set = (int)(it % NSETS);
-            ok = ptx::mbar_wait(&tm_empty[set], (uint32_t)((it / NSETS) & 1) ^ 1u, p.err, 3);
+            ok = wait_or_record(&tm_empty[set], (uint32_t)((it / NSETS) & 1) ^ 1u, p, 3);
             if (!ok) break;
-            ok = ptx::mbar_wait(&full[s], (uint32_t)((it / NSTAGE) & 1), p.err, 4);
+            ok = wait_or_record(&full[s], (uint32_t)((it / NSTAGE) & 1), p, 4);
             if (!ok) break;
             ptx::tc_fence_after();
             const int pcode = stage_path[s];
@@ -944,12 +964,12 @@ emul_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
               }
             }
             ptx::mma_commit(&empty[s]);
-            ptx::mma_commit(&tm_full[set]);
+            if (!(p.hold_first_ready && it == 0)) ptx::mma_commit(&tm_full[set]);
           }
         }
         // drain: all issued MMAs complete before TMEM is released
         ptx::mma_commit(drain);
-        ptx::mbar_wait(drain, 0, p.err, 9);
+        wait_or_record(drain, 0, p, 9, true);
       }
     }
   } else {
@@ -991,14 +1011,14 @@ emul_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
         // overlaps the wait for the block's MMAs (NVFP4's register allocation does worse with it)
         double2 rsv_early = make_double2(0.0, 0.0);
         if constexpr (FMT == EMU_FMT_MXFP4) {
-          ok = __all_sync(0xFFFFFFFFu, ptx::mbar_wait(&cr_full[q], (uint32_t)((it / NCR) & 1), p.err, 6));
+          ok = __all_sync(0xFFFFFFFFu, wait_or_record(&cr_full[q], (uint32_t)((it / NCR) & 1), p, 6));
           if (!ok) break;
           rsv_early = reinterpret_cast<const double2*>(rr_ring + q * RR_BYTES + RR_RS)[rl];
         }
-        ok = __all_sync(0xFFFFFFFFu, ptx::mbar_wait(&tm_full[set], (uint32_t)((it / NSETS) & 1), p.err, 5));
+        ok = __all_sync(0xFFFFFFFFu, wait_or_record(&tm_full[set], (uint32_t)((it / NSETS) & 1), p, 5));
         if (!ok) break;
         if constexpr (FMT != EMU_FMT_MXFP4) {
-          ok = __all_sync(0xFFFFFFFFu, ptx::mbar_wait(&cr_full[q], (uint32_t)((it / NCR) & 1), p.err, 6));
+          ok = __all_sync(0xFFFFFFFFu, wait_or_record(&cr_full[q], (uint32_t)((it / NCR) & 1), p, 6));
           if (!ok) break;
         }
         ptx::tc_fence_after();
@@ -1340,9 +1360,28 @@ static WsLayout layout(int fmt, int64_t M, int64_t N, int64_t K) {
   return L;
 }
 
+std::atomic<long long> g_wait_limit{DRAIN_LIMIT};
+std::atomic<int> g_hold_first_ready{0};
+
 }  // namespace tc
 
 size_t gemm_tc_workspace_size(int fmt, int64_t M, int64_t N, int64_t K) { return tc::layout(fmt, M, N, K).total; }
+
+size_t gemm_tc_path_offset(int fmt, int64_t M, int64_t N, int64_t K) { return tc::layout(fmt, M, N, K).path; }
+
+long long set_wait_limit(long long cycles) {
+  return tc::g_wait_limit.exchange(cycles > 0 ? cycles : tc::DRAIN_LIMIT);
+}
+
+void set_hold_first_ready(int enable) { tc::g_hold_first_ready.store(enable ? 1 : 0); }
+
+cudaError_t take_wait_error(int* code) {
+  *code = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(code, tc::g_wait_error, sizeof(int));
+  if (e != cudaSuccess || *code == 0) return e;
+  const int zero = 0;
+  return cudaMemcpyToSymbol(tc::g_wait_error, &zero, sizeof(int));
+}
 
 bool gemm_tc_supported(int fmt, int w_reduce, int64_t M, int64_t N, int64_t K) {
   using tc::BM;
@@ -1449,6 +1488,8 @@ static cudaError_t run_tc(const uint8_t* A, const uint8_t* B, const uint8_t* SA,
   prm.alpha = alpha;
   prm.out = out;
   prm.err = reinterpret_cast<int*>(ws + L.err);
+  prm.wait_limit = g_wait_limit.load();
+  prm.hold_first_ready = g_hold_first_ready.load();
   prm.r3 = args.stage3_rounding;
   prm.r4 = args.stage4_rounding;
   prm.out_mode = args.out_mode;

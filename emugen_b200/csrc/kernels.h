@@ -39,6 +39,13 @@ cudaError_t launch_gemm_simt(const uint8_t* A, const uint8_t* B, const uint8_t* 
                              const float* alpha, const GemmArgs& args, void* out, cudaStream_t stream);
 
 size_t gemm_tc_workspace_size(int fmt, int64_t M, int64_t N, int64_t K);
+size_t gemm_tc_path_offset(int fmt, int64_t M, int64_t N, int64_t K);
+// pipeline-wait bound of later tensor-core launches (cycles; <= 0 restores 2^31); returns the old one
+long long set_wait_limit(long long cycles);
+// test hook: later tensor-core launches withhold the first accumulator-ready signal (gemm_tc.cu)
+void set_hold_first_ready(int enable);
+// this device's first timed-out wait code since the last call (0 = none), then cleared
+cudaError_t take_wait_error(int* code);
 bool gemm_tc_supported(int fmt, int w_reduce, int64_t M, int64_t N, int64_t K);
 cudaError_t launch_gemm_tc(const uint8_t* A, const uint8_t* B, const uint8_t* SA, const uint8_t* SB,
                            int64_t M, int64_t N, int64_t K, int64_t sa_cols, int64_t sb_cols,
@@ -51,6 +58,16 @@ cudaError_t launch_quant(int sf_vec, const void* x, int dtype, int64_t M, int64_
 // sets emu_last_error() of the calling thread to `message` and returns s (capi.cu)
 int32_t record_failure(int32_t s, const char* message);
 
+// the argument checks of emu_gemm_ws before it looks at the workspace (capi.cu); EMU_OK or the
+// status emu_gemm_ws would return, with emu_last_error() set
+int32_t check_gemm_call(const uint8_t* a_fp4, const uint8_t* b_fp4, const uint8_t* scale_a, const uint8_t* scale_b,
+                        int64_t M, int64_t N, int64_t K, int64_t scale_a_rows, int64_t scale_a_cols,
+                        int64_t scale_b_rows, int64_t scale_b_cols, const emu_gemm_params* params, const void* out);
+
+cudaError_t launch_amax(const void* a, int64_t a_numel, const void* b, int64_t b_numel, int dtype, unsigned* amax_a,
+                        unsigned* amax_b, cudaStream_t stream);
+cudaError_t launch_scales_from_amax(const unsigned* amax_a, const unsigned* amax_b, float* gs_a, float* gs_b,
+                                    float* alpha, cudaStream_t stream);
 cudaError_t launch_global_scales(const void* a, int64_t a_numel, const void* b, int64_t b_numel,
                                  int dtype, float* gs_a, float* gs_b, float* alpha,
                                  cudaStream_t stream);

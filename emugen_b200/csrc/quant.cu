@@ -192,9 +192,12 @@ __global__ void amax_bits_kernel(const T* __restrict__ xa, int64_t na, const T* 
 
 // gs = f32(2688.0 / (amax > 0 ? amax : 1.0)) and alpha = f32(1 / max(gs_a * gs_b, 1e-8)), all in
 // double like the reference's Python floats (gemm_compare/backends/nvfp.py:24-27, 176).
-__global__ void global_scales_finalize(float* gs_a, float* gs_b, float* alpha) {
-  const float aa = __uint_as_float(*reinterpret_cast<unsigned*>(gs_a));
-  const float ab = __uint_as_float(*reinterpret_cast<unsigned*>(gs_b));
+// The amax words may be the gs words themselves (read before written).
+__global__ void global_scales_finalize(const unsigned* amax_a, const unsigned* amax_b, float* gs_a, float* gs_b,
+                                       float* alpha) {
+  const float aa = __uint_as_float(*amax_a);
+  const float ab = __uint_as_float(*amax_b);
+  asm volatile("" ::: "memory");   // both words are read before either output (which may alias them) is written
   const double da = aa > 0.0f ? (double)aa : 1.0;
   const double db = ab > 0.0f ? (double)ab : 1.0;
   const float ga = __double2float_rn(__ddiv_rn(2688.0, da));
@@ -231,10 +234,10 @@ cudaError_t launch_quant(int sf_vec, const void* x, int dtype, int64_t M, int64_
                       : launch_quant_t<32>(x, dtype, M, K, gs, q, sf, stream);
 }
 
-cudaError_t launch_global_scales(const void* a, int64_t a_numel, const void* b, int64_t b_numel, int dtype,
-                                 float* gs_a, float* gs_b, float* alpha, cudaStream_t stream) {
-  cudaError_t err = cudaMemsetAsync(gs_a, 0, sizeof(float), stream);
-  if (err == cudaSuccess) err = cudaMemsetAsync(gs_b, 0, sizeof(float), stream);
+cudaError_t launch_amax(const void* a, int64_t a_numel, const void* b, int64_t b_numel, int dtype, unsigned* amax_a,
+                        unsigned* amax_b, cudaStream_t stream) {
+  cudaError_t err = cudaMemsetAsync(amax_a, 0, sizeof(unsigned), stream);
+  if (err == cudaSuccess) err = cudaMemsetAsync(amax_b, 0, sizeof(unsigned), stream);
   if (err != cudaSuccess) return err;
   // one wave: 4 CTAs of 256 threads per SM and tensor, each thread four 16-byte loads per step
   const int64_t n_max = std::max(a_numel, b_numel);
@@ -246,14 +249,27 @@ cudaError_t launch_global_scales(const void* a, int64_t a_numel, const void* b, 
   const dim3 grid((unsigned)std::min<int64_t>(std::max<int64_t>((n_max / 8 + 1023) / 1024, 1), (int64_t)sms * 4), 2);
   if (dtype == EMU_DTYPE_F16) {
     amax_bits_kernel<__half><<<grid, 256, 0, stream>>>(static_cast<const __half*>(a), a_numel, static_cast<const __half*>(b),
-                                                      b_numel, reinterpret_cast<unsigned*>(gs_a), reinterpret_cast<unsigned*>(gs_b));
+                                                      b_numel, amax_a, amax_b);
   } else {
     amax_bits_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(
-        static_cast<const __nv_bfloat16*>(a), a_numel, static_cast<const __nv_bfloat16*>(b), b_numel,
-        reinterpret_cast<unsigned*>(gs_a), reinterpret_cast<unsigned*>(gs_b));
+        static_cast<const __nv_bfloat16*>(a), a_numel, static_cast<const __nv_bfloat16*>(b), b_numel, amax_a, amax_b);
   }
-  global_scales_finalize<<<1, 1, 0, stream>>>(gs_a, gs_b, alpha);
   return cudaGetLastError();
+}
+
+cudaError_t launch_scales_from_amax(const unsigned* amax_a, const unsigned* amax_b, float* gs_a, float* gs_b,
+                                    float* alpha, cudaStream_t stream) {
+  global_scales_finalize<<<1, 1, 0, stream>>>(amax_a, amax_b, gs_a, gs_b, alpha);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_global_scales(const void* a, int64_t a_numel, const void* b, int64_t b_numel, int dtype,
+                                 float* gs_a, float* gs_b, float* alpha, cudaStream_t stream) {
+  // the amax words live in the gs outputs until the finalize step overwrites them
+  unsigned* wa = reinterpret_cast<unsigned*>(gs_a);
+  unsigned* wb = reinterpret_cast<unsigned*>(gs_b);
+  cudaError_t err = launch_amax(a, a_numel, b, b_numel, dtype, wa, wb, stream);
+  return err != cudaSuccess ? err : launch_scales_from_amax(wa, wb, gs_a, gs_b, alpha, stream);
 }
 
 }  // namespace emu

@@ -39,16 +39,13 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Wait for the phase with the given parity to complete, for at most ~2^31 cycles (about a
-// second at 1.9 GHz).  Returns false on timeout and records `code` in *err (first error wins).
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
+// Wait for the phase with the given parity to complete, for at most `limit` cycles (2^31, the
+// default, is about a second at 1.9 GHz).  Returns false when the limit runs out.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, long long limit) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   while (!mbar_try_wait(bar, parity)) {
-    if (clock64() - t0 > (1ll << 31)) {
-      atomicCAS(err, 0, code);
-      return false;
-    }
+    if (clock64() - t0 > limit) return false;
   }
   return true;
 }

@@ -7,10 +7,13 @@ Mirrors ``RoundStrategy`` / ``coerce_round_strategy`` (rounding.py:10-34), ``Har
 for bit the reference's for the two element formats the reference quantisers produce:
   group_size 16 -> NVFP4 (E4M3 scales as torch.float8_e4m3fn, f32 scale product),
   group_size 32 -> MXFP4 (UE8M0 scales as uint8, f64 scale product).
-The reference lets a caller pass ``unpack_fp4`` / ``linearize_block_scales`` callables; they are
-accepted for signature compatibility, and the element format is taken from ``group_size``, which
-is what the reference's own callers pair them with (gemm_compare/backends/mxfp.py:139-144,
-search/w3.py:139-150).
+The reference lets a caller pass ``unpack_fp4`` / ``linearize_block_scales`` callables
+(core.py:85-101).  The kernels read the packed bytes and swizzled scales themselves, so a callable
+is accepted only when it computes the standard format of the element type chosen by ``group_size``
+-- as the reference's own helpers do, which its callers pass (gemm_compare/backends/mxfp.py:139-144,
+search/w3.py:139-150): e2m1 nibbles low first, and the 128x4 swizzled scales decoded as E4M3
+(group 16) or 2^(u - 127) (group 32).  Each callable is checked once, on a small probe input;
+any other callable raises NotImplementedError instead of being silently ignored.
 """
 from __future__ import annotations
 
@@ -99,6 +102,57 @@ class HardwareConfig:
 CONFIG_RTX_5090 = HardwareConfig.for_rtx_5090()
 
 
+_E2M1 = (0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0, -0.0, -0.5, -1.0, -1.5, -2.0, -3.0, -4.0, -6.0)
+_helper_verdicts: dict = {}
+
+
+def _probe_unpack(fn) -> bool:
+    """Does fn(packed [R, K/2] uint8, (R, K)) unpack e2m1 nibbles, low nibble first?"""
+    packed = torch.arange(256, dtype=torch.int32).to(torch.uint8).reshape(16, 16)
+    lut = torch.tensor(_E2M1)
+    want = torch.stack([lut[(packed & 15).long()], lut[(packed >> 4).long()]], dim=-1).reshape(16, 32)
+    got = fn(packed, (16, 32))
+    return tuple(got.shape) == (16, 32) and bool((got.float().cpu() == want).all())
+
+
+def _probe_linearize(fn, group_size: int) -> bool:
+    """Does fn(swizzled [128, 4] scales, 128, 4) decode the 128x4 swizzled layout to [128, 4] f32
+    values, E4M3 for group 16, 2^(u - 127) for group 32?"""
+    rows, cols = 128, 4
+    lin = (torch.arange(rows * cols, dtype=torch.int64).reshape(rows, cols) * 37 + 11) % 120 + 1  # no NaN codes
+    swz = torch.empty(rows * cols, dtype=torch.uint8)
+    r = torch.arange(rows).reshape(-1, 1)
+    c = torch.arange(cols).reshape(1, -1)
+    off = (r % 32) * 16 + (r // 32) * 4 + c   # one 128-row, 4-column tile of the swizzled layout
+    swz[off.reshape(-1)] = lin.reshape(-1).to(torch.uint8)
+    swz = swz.reshape(rows, cols)
+    if group_size == 16:
+        arg, want = swz.view(torch.float8_e4m3fn), lin.to(torch.uint8).view(torch.float8_e4m3fn).float()
+    else:
+        arg, want = swz, torch.exp2(lin.float() - 127.0)
+    got = fn(arg, rows, cols)
+    return tuple(got.shape) == (rows, cols) and bool((got.float().cpu() == want).all())
+
+
+def _check_helpers(unpack_fp4, linearize_block_scales, group_size: int) -> None:
+    """Raise unless every given callable computes the standard format (module docstring)."""
+    for fn, kind in ((unpack_fp4, "unpack_fp4"), (linearize_block_scales, "linearize_block_scales")):
+        if fn is None:
+            continue
+        key = (fn, kind, group_size)
+        if key not in _helper_verdicts:
+            try:
+                ok = _probe_unpack(fn) if kind == "unpack_fp4" else _probe_linearize(fn, group_size)
+            except Exception:  # a callable that cannot run on the probe is not the standard one either
+                ok = False
+            _helper_verdicts[key] = ok
+        if not _helper_verdicts[key]:
+            raise NotImplementedError(
+                f"{kind}={getattr(fn, '__name__', fn)!r} does not compute the standard "
+                f"{'NVFP4' if group_size == 16 else 'MXFP4'} format; the emulation kernels read packed e2m1 "
+                f"bytes and 128x4 swizzled scales directly and cannot apply a custom {kind}")
+
+
 class MMAEngine:
     """Reference ``MMAEngine`` (core.py:53-148), computed by libemugen.so."""
 
@@ -125,6 +179,7 @@ class MMAEngine:
             fmt = _lib.EMU_FMT_MXFP4
         else:
             raise NotImplementedError(f"group_size {group_size}: only 16 (NVFP4) and 32 (MXFP4) are supported")
+        _check_helpers(unpack_fp4, linearize_block_scales, group_size)
         return _lib.gemm(a_fp4, b_fp4, scale_a, scale_b, fmt=fmt, group_size=group_size, w_reduce=int(w_reduce),
                          stage3_rounding=r3, stage4_rounding=r4, alpha=alpha_tensor, out_mode=out_mode)
 

@@ -1,168 +1,179 @@
-"""Replay of rollout artefacts: the emulated GEMM of every saved case against its saved real output.
+"""Replay of rollout artefacts on the device: the emulated GEMM of every saved case against the real
+output saved with it, on one GPU or split over the ranks of a process group.
 
-``run_suite_import`` mirrors gemm_compare/runner.py:422-526 (same arguments, printout and return
-code: 0 all exact / MSE mode, 1 mismatches, 2 backend mismatch) with the comparison done on the
-device (``emugen_b200.compare``).  ``run_suite_import_sharded`` runs the same replay on every rank of
-an initialised ``torch.distributed`` process group: rank r takes cases r, r + world, ...; the per-case
-results travel in one ``all_reduce(SUM)`` of a float64 [cases, 6] tensor (a case is filled in by
-exactly one rank, zeros elsewhere), and every rank returns the same code; rank 0 prints.
+Artefact format (written by the reference's export harness, gemm_compare/runner.py:299-419 through
+gemm_compare/rollout.py:48-79): one ``torch.save`` file holding a dict with
+  ``gemm_compare_rollout_version``  1
+  ``backend``                       "nvfp" or "mxfp"
+  ``seed``, ``meta``                provenance, echoed in the summary
+  ``cases``                         a list of dicts, each with ``state`` (the backend's quantised
+                                    state dict: gemm_compare/backends/nvfp.py:57-95, mxfp.py:55-94),
+                                    ``real_output`` ([M, N] tensor) and ``M``, ``N``, ``K``,
+                                    ``dist_a``, ``dist_b`` (``iter`` optional).
+``Rollout.read`` checks that shape before any case runs.
+
+Replay (``replay``): rank r of W takes cases r, r + W, ...; every case's verdict goes into one row
+of a float64 [cases, 6] table (zeros on the ranks that did not run it) and the table meets in one
+``all_reduce(SUM)``, so every rank returns the same code: 0 every case exact (or MSE mode), 1 some
+case differs, 2 the artefact's backend is not the requested one (agreed by an all_reduce(MAX)
+first).  Without a process group (or with one rank) the same code runs in this process.  The
+reference's own ``run_suite_import`` (runner.py:422-526) also runs unchanged with this package's
+``emul_fn``; this module adds the device comparison and the split over GPUs.
 """
 from __future__ import annotations
 
 import sys
-import traceback
+from dataclasses import dataclass
 from pathlib import Path
 from typing import Any, Callable
 
 import torch
 
 from .compare import compare_mse, compare_tensors
-from .rollout import load_rollout_artifact, quant_state_from_dict
 
 GemmFn = Callable[[Any], torch.Tensor]
 CompareFn = Callable[..., dict]
 
-# columns of the per-case result rows exchanged between ranks
+FORMAT_VERSION = 1
+_CASE_KEYS = ("state", "real_output", "M", "N", "K")
+
+# columns of the per-case verdict table exchanged between ranks
 _DONE, _MISMATCH, _MAX_DIFF, _MSE_SUM, _MSE_NUMEL, _REF_SQ = range(6)
 
 
-def _replay_case(row: dict[str, Any], idx: int, emul_fn: GemmFn, backend: str, device: str, metric_mode: str,
-                 sample_count: int, cmp_exact: CompareFn, cmp_mse: CompareFn) -> dict[str, Any]:
-    state = quant_state_from_dict(row["state"], backend, device=device)
-    real_output = row["real_output"].to(device)
-    modeling_res = emul_fn(state)
+@dataclass(frozen=True)
+class Rollout:
+    """A rollout artefact read from disk (tensors on the CPU)."""
+
+    backend: str
+    seed: Any
+    meta: dict
+    cases: list
+
+    @classmethod
+    def read(cls, path: str | Path) -> "Rollout":
+        """Load and validate an artefact.  Raises ValueError for any other version or a missing field."""
+        blob = torch.load(path, map_location="cpu", weights_only=False)
+        if not isinstance(blob, dict):
+            raise ValueError(f"{path}: not a rollout artefact (a {type(blob).__name__}, not a dict)")
+        version = blob.get("gemm_compare_rollout_version")
+        if version != FORMAT_VERSION:
+            raise ValueError(f"{path}: rollout format version {version!r}, this reader handles {FORMAT_VERSION}")
+        backend, cases = blob.get("backend"), blob.get("cases")
+        if not isinstance(backend, str) or not isinstance(cases, list):
+            raise ValueError(f"{path}: rollout artefact without a backend name or a case list")
+        for i, case in enumerate(cases):
+            missing = [k for k in _CASE_KEYS if k not in case]
+            if missing:
+                raise ValueError(f"{path}: case {i} lacks {', '.join(missing)}")
+        return cls(backend.lower(), blob.get("seed"), dict(blob.get("meta") or {}), cases)
+
+    def state(self, i: int, device: str | torch.device):
+        """The quantised state of case i, rebuilt by its backend's deserialiser on `device`."""
+        if self.backend == "nvfp":
+            from .backends.nvfp import nvfp_quant_state_from_dict as from_dict
+        elif self.backend == "mxfp":
+            from .backends.mxfp import mxfp_quant_state_from_dict as from_dict
+        else:
+            raise ValueError(f"rollout backend {self.backend!r} is neither 'nvfp' nor 'mxfp'")
+        return from_dict(self.cases[i]["state"], device=device)
+
+
+def _verdict_row(case: dict, state, emul_fn: GemmFn, device, metric_mode: str, sample_count: int,
+                 cmp_exact: CompareFn, cmp_mse: CompareFn) -> tuple[torch.Tensor, dict]:
+    real = case["real_output"].to(device)
+    emulated = emul_fn(state)
+    row = torch.zeros(6, dtype=torch.float64)
+    row[_DONE] = 1.0
     if metric_mode == "exact":
-        cmp = cmp_exact(real_output, modeling_res, sample_count=sample_count)
+        c = cmp_exact(real, emulated, sample_count=sample_count)
+        row[_MISMATCH] = 1.0 if c["status"] == "MISMATCH" else 0.0
+        row[_MAX_DIFF] = float(c["max_diff"])
     elif metric_mode == "mse":
-        cmp = cmp_mse(real_output, modeling_res)
+        c = cmp_mse(real, emulated)
+        row[_MSE_SUM], row[_MSE_NUMEL] = float(c["mse_sum"]), float(c["mse_numel"])
+        row[_REF_SQ], row[_MAX_DIFF] = float(c["real_sq_sum"]), float(c["max_mse"])
     else:
         raise ValueError(f"unknown metric_mode={metric_mode!r}")
-    return {"iter": row.get("iter", idx), "M": row["M"], "N": row["N"], "K": row["K"], "dist_a": row["dist_a"],
-            "dist_b": row["dist_b"], **cmp}
+    return row, c
 
 
-def _summary(name: str, n_cases: int, results: list[dict[str, Any]], metric_mode: str) -> int:
-    print("\n" + "=" * 70)
-    print(f"SUMMARY | {name}")
-    print("=" * 70)
+def _report(title: str, rollout: Rollout, table: torch.Tensor, metric_mode: str) -> None:
+    done = table[:, _DONE] > 0
+    n, ran = table.shape[0], int(done.sum())
+    print(f"{title}: {ran}/{n} cases replayed (backend {rollout.backend}, artefact seed {rollout.seed})")
     if metric_mode == "mse":
-        total_numel = sum(int(r.get("mse_numel", 0)) for r in results)
-        total_mse_sum = sum(float(r.get("mse_sum", 0.0)) for r in results)
-        mean_mse = total_mse_sum / max(total_numel, 1)
-        per_gemm = [float(r.get("per_gemm_rel_l2_error", 0.0)) for r in results]
-        mean_per_gemm = sum(per_gemm) / max(len(per_gemm), 1)
-        worst = max((float(r.get("max_mse", 0.0)) for r in results), default=0.0)
-        print(f"Total: {n_cases}, Completed: {len(results)}")
-        print(f"MSE mean: {mean_mse:.8e}")
-        print(f"mean over GEMMs of sqrt(sum(error^2)) / sqrt(sum(real^2)): {mean_per_gemm:.8e}")
-        print(f"MSE max (worst element): {worst:.8e}")
-        return 0
-    mismatches = [r for r in results if r["status"] == "MISMATCH"]
-    print(f"Total: {n_cases}, Matches: {len(results) - len(mismatches)}, Mismatches: {len(mismatches)}")
-    print("=" * 70)
-    if not mismatches:
-        print("*** All tests: exact bitwise match ***")
-        return 0
-    print(f"Exact-match rate: {(len(results) - len(mismatches)) / max(len(results), 1) * 100:.2f}%")
-    return 1
+        numel = float(table[done, _MSE_NUMEL].sum())
+        rel = [float(s) ** 0.5 / max(float(r) ** 0.5, 1e-12) for s, r in zip(table[done, _MSE_SUM], table[done, _REF_SQ])]
+        print(f"  MSE {float(table[done, _MSE_SUM].sum()) / max(numel, 1.0):.8e}, "
+              f"mean relative L2 error {sum(rel) / max(len(rel), 1):.8e}, "
+              f"worst element {float(table[done, _MAX_DIFF].max()) if ran else 0.0:.8e}")
+        return
+    bad = [i for i in range(n) if done[i] and table[i, _MISMATCH] > 0]
+    print(f"  bit-exact: {ran - len(bad)}, differing: {len(bad)}" +
+          (f" (cases {bad[:20]}{' ...' if len(bad) > 20 else ''})" if bad else ""))
 
 
-def _load_checked(artifact_path, backend: str):
-    data = load_rollout_artifact(artifact_path, map_location="cpu")
-    art_backend = str(data["backend"]).lower()
-    if art_backend != backend.lower():
-        print(f"ERROR: artifact backend {art_backend!r} != CLI backend {backend.lower()!r}", file=sys.stderr)
-        return None
-    return data
-
-
-def run_suite_import(emul_fn: GemmFn, *, backend: str, artifact_path: str | Path, name: str = "GEMM compare import",
-                     device: str = "cuda", sample_count: int = 5, max_mismatch_print: int = 20,
-                     metric_mode: str = "exact", print_iter_status: bool = True,
-                     compare_fn: CompareFn = compare_tensors, mse_fn: CompareFn = compare_mse) -> int:
-    """Replay a saved rollout on this device and compare with the saved real outputs."""
-    data = _load_checked(artifact_path, backend)
-    if data is None:
-        return 2
-    cases: list[dict[str, Any]] = list(data["cases"])
-    print(f"\n{'=' * 70}\n{name}\n{'=' * 70}")
-    print(f"Mode: IMPORT <- {artifact_path}")
-    print(f"artifact seed = {data.get('seed')}")
-    print(f"artifact meta = {data.get('meta', {})}")
-    print(f"Cases: {len(cases)} | device = {device}")
-    print("=" * 70)
-    results: list[dict[str, Any]] = []
-    printed = 0
-    for idx, row in enumerate(cases):
-        print(f"\rImport {idx + 1}/{len(cases)}: iter={row.get('iter')} ... ", end="")
-        sys.stdout.flush()
-        try:
-            out = _replay_case(row, idx, emul_fn, backend, device, metric_mode, sample_count, compare_fn, mse_fn)
-            results.append(out)
-            print(out["status"] if print_iter_status else "OK")
-            if metric_mode == "exact" and out["status"] == "MISMATCH" and printed < max_mismatch_print:
-                printed += 1
-                print("    >>> Mismatch Details:")
-                for d in out["mismatch_details"]:
-                    print(f"      Pos {d['idx']}: Real={d['real']:.6f} | Model={d['model']:.6f} | Diff={d['diff']:.6f}")
-        except Exception as e:  # reported per case, as the reference does
-            print(f"\nFATAL ERROR on import case {idx + 1}: {e}")
-            traceback.print_exc()
-    return _summary(name, len(cases), results, metric_mode)
-
-
-def run_suite_import_sharded(emul_fn: GemmFn, *, backend: str, artifact_path: str | Path,
-                             name: str = "GEMM compare import (sharded)", device: str = "cuda",
-                             sample_count: int = 5, metric_mode: str = "exact",
-                             compare_fn: CompareFn = compare_tensors, mse_fn: CompareFn = compare_mse,
-                             group=None) -> int:
-    """run_suite_import over all ranks of the default (or given) process group."""
+def replay(emul_fn: GemmFn, *, backend: str, artifact_path: str | Path, device: str = "cuda",
+           metric_mode: str = "exact", sample_count: int = 5, compare_fn: CompareFn = compare_tensors,
+           mse_fn: CompareFn = compare_mse, group=None, distributed: bool = True,
+           title: str = "rollout replay") -> int:
+    """Replay an artefact with `emul_fn`, split over `group`'s ranks when `distributed` and a process
+    group is initialised (every rank must then call this), else in this process alone.  Returns
+    0 / 1 / 2 (module doc)."""
     import torch.distributed as dist
 
-    rank, world = dist.get_rank(group), dist.get_world_size(group)
-    data = _load_checked(artifact_path, backend)
-    bad_backend = torch.tensor([0.0 if data is not None else 1.0], dtype=torch.float64)
-    cases: list[dict[str, Any]] = list(data["cases"]) if data is not None else []
-    n = torch.tensor([float(len(cases))], dtype=torch.float64)
-    comm_dev = torch.device("cuda", torch.cuda.current_device()) if dist.get_backend(group) == "nccl" else "cpu"
-    head = torch.cat([bad_backend, n]).to(comm_dev)
-    dist.all_reduce(head, op=dist.ReduceOp.MAX, group=group)   # every rank sees the same verdict
-    if head[0].item() > 0:
+    split = distributed and dist.is_available() and dist.is_initialized()
+    rank, world = (dist.get_rank(group), dist.get_world_size(group)) if split else (0, 1)
+    try:
+        rollout = Rollout.read(artifact_path)
+        wrong_backend = rollout.backend != backend.lower()
+    except (OSError, ValueError) as e:
+        print(f"[rank {rank}] cannot replay {artifact_path}: {e}", file=sys.stderr)
+        rollout, wrong_backend = None, True
+    comm = (torch.device("cuda", torch.cuda.current_device())
+            if split and dist.get_backend(group) == "nccl" else torch.device("cpu"))
+    if split:
+        flag = torch.tensor([1.0 if wrong_backend else 0.0], dtype=torch.float64, device=comm)
+        dist.all_reduce(flag, op=dist.ReduceOp.MAX, group=group)   # one verdict for all ranks
+        wrong_backend = bool(flag.item() > 0)
+    if wrong_backend:
+        if rank == 0 and rollout is not None:
+            print(f"ERROR: artifact backend {rollout.backend!r} != requested backend {backend.lower()!r}",
+                  file=sys.stderr)
         return 2
-    table = torch.zeros((len(cases), 6), dtype=torch.float64)
-    for idx in range(rank, len(cases), world):
-        row = cases[idx]
+    table = torch.zeros((len(rollout.cases), 6), dtype=torch.float64)
+    for i in range(rank, len(rollout.cases), world):
         try:
-            out = _replay_case(row, idx, emul_fn, backend, device, metric_mode, sample_count, compare_fn, mse_fn)
-        except Exception as e:
-            print(f"[rank {rank}] FATAL ERROR on import case {idx + 1}: {e}", file=sys.stderr)
-            continue
-        table[idx, _DONE] = 1.0
-        if metric_mode == "exact":
-            table[idx, _MISMATCH] = 1.0 if out["status"] == "MISMATCH" else 0.0
-            table[idx, _MAX_DIFF] = float(out["max_diff"])
-        else:
-            table[idx, _MSE_SUM] = float(out["mse_sum"])
-            table[idx, _MSE_NUMEL] = float(out["mse_numel"])
-            table[idx, _REF_SQ] = float(out["real_sq_sum"])
-            table[idx, _MAX_DIFF] = float(out["max_mse"])
-    t = table.to(comm_dev)
-    dist.all_reduce(t, op=dist.ReduceOp.SUM, group=group)
-    table = t.cpu()
-    results: list[dict[str, Any]] = []
-    for idx in range(len(cases)):
-        if table[idx, _DONE] == 0:
-            continue
-        if metric_mode == "exact":
-            results.append({"status": "MISMATCH" if table[idx, _MISMATCH] > 0 else "SUCCESS",
-                            "max_diff": float(table[idx, _MAX_DIFF])})
-        else:
-            s, ne, rs = (float(table[idx, c]) for c in (_MSE_SUM, _MSE_NUMEL, _REF_SQ))
-            results.append({"status": "OK", "mse_sum": s, "mse_numel": int(ne), "real_sq_sum": rs,
-                            "max_mse": float(table[idx, _MAX_DIFF]),
-                            "per_gemm_rel_l2_error": (s ** 0.5) / max(rs ** 0.5, 1e-12)})
+            table[i], _ = _verdict_row(rollout.cases[i], rollout.state(i, device), emul_fn, device, metric_mode,
+                                       sample_count, compare_fn, mse_fn)
+        except Exception as e:  # reported per case; the case stays out of the verdict
+            print(f"[rank {rank}] case {i}: {type(e).__name__}: {e}", file=sys.stderr)
+    if split:
+        t = table.to(comm)
+        dist.all_reduce(t, op=dist.ReduceOp.SUM, group=group)
+        table = t.cpu()
     if rank == 0:
-        return _summary(name, len(cases), results, metric_mode)
+        _report(title, rollout, table, metric_mode)
     if metric_mode == "mse":
         return 0
-    return 1 if any(r["status"] == "MISMATCH" for r in results) else 0
+    return 1 if bool((table[:, _MISMATCH] > 0).any()) else 0
+
+
+def run_suite_import(emul_fn: GemmFn, *, backend: str, artifact_path: str | Path, device: str = "cuda",
+                     sample_count: int = 5, metric_mode: str = "exact", compare_fn: CompareFn = compare_tensors,
+                     mse_fn: CompareFn = compare_mse, **_ignored) -> int:
+    """Single-process replay with the arguments and return codes of the reference's
+    ``run_suite_import`` (gemm_compare/runner.py:422-433); printing options are accepted and ignored."""
+    return replay(emul_fn, backend=backend, artifact_path=artifact_path, device=device, sample_count=sample_count,
+                  metric_mode=metric_mode, compare_fn=compare_fn, mse_fn=mse_fn, distributed=False)
+
+
+def run_suite_import_sharded(emul_fn: GemmFn, *, backend: str, artifact_path: str | Path, device: str = "cuda",
+                             sample_count: int = 5, metric_mode: str = "exact", compare_fn: CompareFn = compare_tensors,
+                             mse_fn: CompareFn = compare_mse, group=None, **_ignored) -> int:
+    """``replay`` over the ranks of the default (or given) process group."""
+    return replay(emul_fn, backend=backend, artifact_path=artifact_path, device=device, metric_mode=metric_mode,
+                  sample_count=sample_count, compare_fn=compare_fn, mse_fn=mse_fn, group=group,
+                  title="rollout replay (sharded)")
+

@@ -48,7 +48,8 @@ enum {
   EMU_ERR_SCALE_SHAPE = 6,        /* "swizzled scale shape must be divisible by 128 and 4"        */
   EMU_ERR_SCALE_TOO_SMALL = 7,    /* scale buffer has fewer rows / columns than M,N / K/group     */
   EMU_ERR_UNSUPPORTED = 8,        /* a size beyond what this library supports (message says which) */
-  EMU_ERR_CUDA = 9                /* a CUDA runtime error (message carries cudaGetErrorString)    */
+  EMU_ERR_CUDA = 9,               /* a CUDA runtime error (message carries cudaGetErrorString)    */
+  EMU_ERR_TIMEOUT = 10            /* a tensor-core pipeline wait ran out (emu_device_status)       */
 };
 
 /* Element formats. */
@@ -119,6 +120,15 @@ EMU_API size_t emu_gemm_workspace_size(int64_t M, int64_t N, int64_t K, const em
 EMU_API size_t emu_gemm_tc_workspace_size(int64_t M, int64_t N, int64_t K, const emu_gemm_params* params);
 
 /*
+ * Diagnostic: byte offset, within the tensor-core path's workspace, of its per-block epilogue path
+ * codes ((size_t)-1 where that path does not apply).  After a call on that path completes,
+ * workspace[offset + (tm * tiles_n + tn) * (K / 64) + kb] holds the code of 128-row tile tm,
+ * 64-column tile tn (tiles_n = ceil(N / 64)) and 64-wide K block kb: bits 0-1 = 0 f64, 1 integer,
+ * 2 block-sum, 3 mixed (the exactness classes the kernel chose).  No reference counterpart.
+ */
+EMU_API size_t emu_gemm_tc_path_offset(int64_t M, int64_t N, int64_t K, const emu_gemm_params* params);
+
+/*
  * emu_gemm with caller-provided scratch: `workspace` (1024-byte aligned, at least
  * emu_gemm_workspace_size bytes, contents need not be initialised) enables the tcgen05 path; with
  * workspace == NULL the call is exactly emu_gemm.  Same results bit for bit either way.
@@ -163,7 +173,36 @@ EMU_API emu_status emu_gemm_model(const uint8_t* a_fp4, const uint8_t* b_fp4, co
                                   const emu_accum_model* model, void* out, void* stream);
 
 /*
- * Bytes of the per-device static scratch behind emu_gemm_static (64 MiB).
+ * Status of the asynchronous work on this device: synchronises `stream`, then reads and clears the
+ * device's record of tensor-core pipeline waits that ran out.  Every wait in that kernel is
+ * bounded (emu_set_wait_limit); a wait that runs out makes the kernel stop, drain the copies and
+ * MMAs it has in flight, free its tensor memory and return, leaving the outputs of the unfinished
+ * tiles undefined.  Returns EMU_OK, EMU_ERR_TIMEOUT (the message names the wait) or EMU_ERR_CUDA.
+ * The reference raises synchronously on bad input (nvfp_emulation.cpp:99-106); this is the
+ * asynchronous counterpart for failures that only the device can see.
+ */
+EMU_API emu_status emu_device_status(void* stream);
+
+/*
+ * Bound, in SM clock cycles, of each pipeline wait of the tensor-core kernels launched after this
+ * call, process-wide (<= 0 restores the default 2^31, about a second); returns the previous bound.
+ * Waits for copies or MMAs already in flight at exit always use the default.  No reference
+ * counterpart (the reference has no device pipeline).
+ */
+EMU_API int64_t emu_set_wait_limit(int64_t cycles);
+
+/*
+ * Test hook for the failure path, process-wide: while enabled, tensor-core launches withhold their
+ * first accumulator-ready signal, so the epilogue's bounded wait runs out (no fault, no hang; the
+ * kernel returns and emu_device_status reports EMU_ERR_TIMEOUT).  Never enable it in production.
+ */
+EMU_API emu_status emu_test_hold_first_ready(int32_t enable);
+
+/*
+ * Bytes of the per-device static scratch behind emu_gemm_static (64 MiB).  The array belongs to the
+ * library's device module: every device on which that module is loaded holds it (64 MiB + 1 KiB)
+ * until the process exits, whether or not emu_gemm_static is called -- at library load under
+ * CUDA_MODULE_LOADING=EAGER, else when the module is first used on the device.
  */
 #define EMU_STATIC_SCRATCH_BYTES (64u << 20)
 
@@ -174,10 +213,12 @@ EMU_API emu_status emu_gemm_model(const uint8_t* a_fp4, const uint8_t* b_fp4, co
  * processes whose memory pools already hold the device).  Problems taking the CUDA-core path run
  * it (it needs no scratch).  No reference counterpart: the reference allocates its outputs and
  * temporaries through torch.
- *   - Problems whose emu_gemm_workspace_size exceeds EMU_STATIC_SCRATCH_BYTES fail with
- *     EMU_ERR_UNSUPPORTED (use emu_gemm_ws).
- *   - The first call on each device, with that device current, resolves the scratch address
- *     (cudaGetSymbolAddress, which may load the library's module); make it before any stream capture.
+ *   - The arguments are checked first, exactly as emu_gemm checks them (same status codes and
+ *     messages); then problems whose emu_gemm_workspace_size exceeds EMU_STATIC_SCRATCH_BYTES fail
+ *     with EMU_ERR_UNSUPPORTED (use emu_gemm_ws).
+ *   - Every call looks up the scratch's device address on the current device
+ *     (cudaGetSymbolAddress; nothing is cached, so a device reset cannot leave a stale address).
+ *     The first call on a device may load the library's module: make it before any stream capture.
  *   - One scratch per device: calls whose executions overlap on a device (different streams or
  *     threads) race on it and must be serialised by the caller.
  *   - Nothing needs to be zeroed beforehand: each call clears its own flag words on `stream`.
@@ -198,6 +239,20 @@ EMU_API emu_status emu_gemm_static(const uint8_t* a_fp4, const uint8_t* b_fp4, c
 EMU_API emu_status emu_nvfp4_global_scales(const void* a, int64_t a_numel, const void* b, int64_t b_numel,
                                    int32_t dtype, float* gs_a, float* gs_b, float* alpha,
                                    void* stream);
+
+/*
+ * The two halves of emu_nvfp4_global_scales, for operands sharded over several devices.
+ * emu_nvfp4_amax writes max|x| of a and of b as the bits of a non-negative f32 (device uint32[1]
+ * each; unsigned order is value order, a NaN input gives a NaN pattern above +inf), so the words of
+ * several shards combine with an integer MAX (e.g. an NCCL all_reduce MAX) into the amax of the
+ * whole operand.  emu_nvfp4_scales_from_amax turns two such words into gs_a, gs_b and alpha exactly
+ * as emu_nvfp4_global_scales does (the words may alias gs_a / gs_b).  Together they replace
+ * gemm_compare/backends/nvfp.py:24-27 global_scale_nvfp and nvfp.py:174-177 for a sharded caller.
+ */
+EMU_API emu_status emu_nvfp4_amax(const void* a, int64_t a_numel, const void* b, int64_t b_numel, int32_t dtype,
+                                  uint32_t* amax_a, uint32_t* amax_b, void* stream);
+EMU_API emu_status emu_nvfp4_scales_from_amax(const uint32_t* amax_a, const uint32_t* amax_b, float* gs_a,
+                                              float* gs_b, float* alpha, void* stream);
 
 /*
  * NVFP4 quantisation: x [M][K] fp16/bf16 -> q [M][K/2] packed e2m1, sf [pad128(M)][pad4(K/16)]

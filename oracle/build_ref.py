@@ -37,10 +37,13 @@ def build(reference: Path, out: Path, verbose: bool = False) -> dict[str, Path]:
 
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("EMUGEN_REFERENCE"),
+                    help="root of the reference source tree (default: $EMUGEN_REFERENCE)")
     ap.add_argument("--out", default=str(Path(__file__).resolve().parent / "_ref"))
     ap.add_argument("--verbose", action="store_true")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("give --reference or set EMUGEN_REFERENCE")
     ref = Path(args.reference)
     if not ref.is_dir():
         print(f"reference tree not present at {ref}; nothing to build", file=sys.stderr)

@@ -11,11 +11,12 @@ quantiser (a test helper; the quantiser is not under test here), plus the edge c
 arithmetic has: NaN E4M3 scales, UE8M0 0 and 255, all -0 inputs, fp16 overflow, f32-subnormal
 accumulators, RZ saturation at FLT_MAX, K=64 (one block), M=1, stage-1 fp16 rounding, odd M/N.
 
-Run:  python tests/golden/make_golden.py --reference /root/reference
+Run:  python tests/golden/make_golden.py --reference <reference tree>   (or set EMUGEN_REFERENCE)
 """
 from __future__ import annotations
 
 import argparse
+import os
 import json
 import sys
 from pathlib import Path
@@ -153,6 +154,13 @@ def make_cases(rng: np.random.Generator) -> list[dict]:
     add(kind="mxfp", path="py", M=64, N=48, K=512, data="student_t", r3=1, r4=1, w_reduce=4, out="bfloat16")
     add(kind="mxfp", path="py", M=33, N=17, K=256, data="huge_bf16", r3=0, r4=0, w_reduce=2, out="bfloat16")
     add(kind="mxfp", path="py", M=16, N=16, K=128, data="normal", r3=0, r4=0, w_reduce=1, out="float16")
+    # --- tensor-core shapes (>= 2^27 multiply-accumulates, M >= 128, N >= 64, K % 64 == 0), C++ emulators:
+    # outlier channels (block-sum / mixed / integer epilogue paths), plain normal data under RNE, MXFP4
+    # normal and Student-t(3)
+    add(kind="nvfp", path="cpp", M=512, N=512, K=512, data="abs_normal", r3=0, r4=0)
+    add(kind="nvfp", path="cpp", M=512, N=512, K=512, data="normal", r3=1, r4=1)
+    add(kind="mxfp", path="cpp", M=512, N=512, K=1024, data="normal", r3=0, r4=0)
+    add(kind="mxfp", path="cpp", M=512, N=512, K=1024, data="student_t", r3=1, r4=0)
     return cases
 
 
@@ -303,7 +311,8 @@ def run_reference(case, a, b, sfa, sfb, alpha, reference: Path):
 
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("EMUGEN_REFERENCE"),
+                    help="root of the reference source tree (default: $EMUGEN_REFERENCE)")
     ap.add_argument("--seed", type=int, default=20261201)
     args = ap.parse_args()
     reference = Path(args.reference)

@@ -73,3 +73,19 @@ def test_quant_validation():
     assert L.emu_quant_mxfp4(fake, 0, 4, 48, fake, fake, None) == 3
     assert L.emu_quant_mxfp4(fake, 7, 4, 64, fake, fake, None) == 1
     assert L.emu_quant_nvfp4(fake, 0, 4, 64, None, fake, fake, None) == 1
+
+
+def test_wait_limit_and_status_names():
+    """The pipeline-wait bound is a process-wide setting that returns the previous value (no device
+    call); EMU_ERR_TIMEOUT has a name."""
+    L = _lib.load()
+    default = 1 << 31
+    prev = L.emu_set_wait_limit(1000)
+    try:
+        assert prev == default
+        assert L.emu_set_wait_limit(-5) == 1000
+        assert L.emu_set_wait_limit(0) == default
+    finally:
+        L.emu_set_wait_limit(prev)
+    assert L.emu_status_string(_lib.EMU_ERR_TIMEOUT) == b"EMU_ERR_TIMEOUT"
+    assert L.emu_test_hold_first_ready(0) == _lib.EMU_OK

@@ -145,7 +145,8 @@ def test_pseudo_fn_is_dequant_then_matmul(backend):
 
 
 def test_replay_through_emulated_gemm(tmp_path):
-    from emugen_b200 import replay, rollout
+    from emugen_b200 import replay
+    from tests.test_replay_cpu import write_rollout
     from emugen_b200.backends.nvfp import build_nvfp_fns, nvfp_quant_state_to_cpu_dict
 
     quant_fn, _real, emul_fn, _meta = build_nvfp_fns()
@@ -161,11 +162,11 @@ def test_replay_through_emulated_gemm(tmp_path):
         cases.append({"iter": i, "M": M, "N": N, "K": K, "dist_a": "normal", "dist_b": "normal",
                       "state": nvfp_quant_state_to_cpu_dict(st), "real_output": real})
     p = tmp_path / "roll.pt"
-    rollout.save_rollout_artifact(p, backend="nvfp", meta={}, seed=0, cases=cases)
+    write_rollout(p, backend="nvfp", cases=cases)
     assert replay.run_suite_import(emul_fn, backend="nvfp", artifact_path=p) == 1
     assert replay.run_suite_import(emul_fn, backend="nvfp", artifact_path=p, metric_mode="mse") == 0
     del cases[1]
-    rollout.save_rollout_artifact(p, backend="nvfp", meta={}, seed=0, cases=cases)
+    write_rollout(p, backend="nvfp", cases=cases)
     assert replay.run_suite_import(emul_fn, backend="nvfp", artifact_path=p) == 0
 
 

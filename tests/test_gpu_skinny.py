@@ -66,7 +66,7 @@ def test_skinny_vs_oracle_and_general_kernel(kind, data, M, N, K, wr, r3, r4, ou
 
 
 def test_decode_shape_timing_smoke():
-    """The config-4 decode shapes run (timed in DESIGN with this kernel): M = 1, 8, 32 x (N, K) =
+    """The decode shapes of the benchmark configuration run: M = 1, 8, 32 x (N, K) =
     (128256, 4096), sampled columns checked against the oracle."""
     from emugen_b200 import _lib
     from tests.golden.make_golden import pad, swizzle

@@ -9,7 +9,7 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from emugen_b200 import replay, rollout
+from emugen_b200 import replay
 from emugen_b200.backends.nvfp import NVFPQuantState, nvfp_quant_state_to_cpu_dict
 
 BAD_ALPHA = 0.125   # the case whose emulation is perturbed by the fake emulator below
@@ -58,21 +58,34 @@ def _make_artifact(path, n_cases=5, bad=(3,)):
         real = (st.a_fp4.float() @ st.b_fp4.float().T / 64.0).to(torch.float16)
         cases.append({"iter": i, "M": M, "N": N, "K": K, "dist_a": "normal", "dist_b": "normal",
                       "state": nvfp_quant_state_to_cpu_dict(st), "real_output": real})
-    rollout.save_rollout_artifact(path, backend="nvfp", meta={"note": "test"}, seed=7, cases=cases)
+    write_rollout(path, backend="nvfp", meta={"note": "test"}, seed=7, cases=cases)
 
 
-def test_artifact_round_trip(tmp_path):
+def write_rollout(path, *, backend, cases, seed=0, meta=None, version=1):
+    """An artefact in the format the reference's export harness writes (gemm_compare/rollout.py:48-79)."""
+    torch.save({"gemm_compare_rollout_version": version, "backend": backend, "meta": meta or {}, "seed": seed,
+                "cases": cases}, path)
+
+
+def test_artifact_reader(tmp_path):
     p = tmp_path / "r.pt"
     _make_artifact(p)
-    d = rollout.load_rollout_artifact(p)
-    assert d["gemm_compare_rollout_version"] == 1 and d["backend"] == "nvfp" and d["seed"] == 7
-    assert len(d["cases"]) == 5
-    st = rollout.quant_state_from_dict(d["cases"][0]["state"], "nvfp", device="cpu")
+    r = replay.Rollout.read(p)
+    assert r.backend == "nvfp" and r.seed == 7 and r.meta == {"note": "test"} and len(r.cases) == 5
+    st = r.state(0, device="cpu")
     assert st.a_fp4.shape == (8, 32) and st.out_dtype == torch.float16
-    with pytest.raises(ValueError):
-        bad = tmp_path / "bad.pt"
-        torch.save({"gemm_compare_rollout_version": 99, "backend": "nvfp", "cases": []}, bad)
-        rollout.load_rollout_artifact(bad)
+    bad = tmp_path / "bad.pt"
+    write_rollout(bad, backend="nvfp", cases=[], version=99)
+    with pytest.raises(ValueError, match="version 99"):
+        replay.Rollout.read(bad)
+    write_rollout(bad, backend="nvfp", cases=[{"M": 1}])
+    with pytest.raises(ValueError, match="case 0 lacks state"):
+        replay.Rollout.read(bad)
+    torch.save([1, 2], bad)
+    with pytest.raises(ValueError, match="not a rollout"):
+        replay.Rollout.read(bad)
+    # an unreadable artefact is reported as code 2, like a backend mismatch
+    assert replay.run_suite_import(_fake_gemm, backend="nvfp", artifact_path=bad, device="cpu") == 2
 
 
 def test_single_process_replay_codes(tmp_path):

@@ -28,7 +28,16 @@ def test_static_entry_exported_and_rejects_oversized_problems():
     M = N = K = 4096
     need = L.emu_gemm_workspace_size(M, N, K, ctypes.byref(prm))
     assert need > _lib.STATIC_SCRATCH_BYTES
+    # the argument checks come first: NULL tensors are reported exactly as emu_gemm reports them
     st = L.emu_gemm_static(None, None, None, None, M, N, K, M, K // 16, N, K // 16, None, ctypes.byref(prm), None, None)
+    st_ref = L.emu_gemm(None, None, None, None, M, N, K, M, K // 16, N, K // 16, None, ctypes.byref(prm), None, None)
+    assert st == st_ref == 1  # EMU_ERR_INVALID_ARGUMENT
+    assert "NULL" in L.emu_last_error().decode()
+    # valid-looking (16-byte aligned, never dereferenced) pointers: the size limit rejects the problem
+    # on the host, before anything is enqueued
+    host = np.zeros(64, dtype=np.uint8)
+    p = (host.ctypes.data + 15) // 16 * 16
+    st = L.emu_gemm_static(p, p, p, p, M, N, K, M, K // 16, N, K // 16, None, ctypes.byref(prm), p, None)
     assert st == 8  # EMU_ERR_UNSUPPORTED
     msg = L.emu_last_error().decode()
     assert "needs" in msg and str(need) in msg and str(_lib.STATIC_SCRATCH_BYTES) in msg
