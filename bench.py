@@ -8,8 +8,12 @@ data, drawn on the CPU and moved to the GPU.  One step = the public path a calle
 ``emul_fn(state)`` (the emulated GEMM, fp16 out as the reference NVFP emulator returns).
 ``value`` is M*N*K per step with inputs resident in HBM; ``e2e`` adds, every step, the host->device
 copy of A, B from pinned memory and the device->host copy of the output, on copy streams that
-overlap the neighbouring steps' compute (double-buffered device inputs).  Multi-GPU: every rank runs
-its own seeded case (weak scaling); timing is the max over ranks of CUDA-event time.
+overlap the neighbouring steps' compute (double-buffered device inputs).  Multi-GPU (torchrun, one
+process per GPU): the same single GEMM per step, split by output columns (strong scaling) -- rank r
+holds all of A and its rows of B, takes the global scale of B from every rank's amax (one all_reduce
+MAX of two words) and computes its columns of C; an all_gather of C is timed separately, and the
+earlier mode (an independent seeded case per GPU, weak scaling) is reported beside it.  Timing is
+the max over ranks of CUDA-event time.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--mnk M,N,K]
 
@@ -444,18 +448,34 @@ def main() -> int:
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
 
+    from emugen_b200 import _lib, shard
     from emugen_b200.backends.nvfp import build_nvfp_fns
 
     quant_fn, _real_fn, emul_fn, _meta = build_nvfp_fns(out_dtype=torch.bfloat16)
-    a_h, b_h = make_inputs(rank)
-    a_d, b_d = a_h.to(dev), b_h.to(dev)
     stream = torch.cuda.current_stream(dev)
+    # one GEMM for the whole job: rank r holds all of A and rows [n0, n1) of B (output columns n0..n1)
+    n0, n1 = shard.column_range(N, world, rank)
+    a_h, b_full_h = make_inputs(0)
+    b_h = b_full_h[n0:n1].contiguous()
+    a_d, b_d = a_h.to(dev), b_h.to(dev)
 
     def step(a, b, ev=None):
-        st = quant_fn(a, b)
-        if ev is not None:
-            ev[0].record(stream)
-        out = emul_fn(st)
+        """quant_fn + emul_fn of this rank's share.  One GPU: the drop-in builders, unchanged.  Several:
+        the global scale of B from all ranks' amax (one all_reduce MAX of two words), then A and this
+        rank's B rows quantised and the emulated GEMM of C[:, n0:n1]."""
+        if world == 1:
+            st = quant_fn(a, b)
+            if ev is not None:
+                ev[0].record(stream)
+            out = emul_fn(st)
+        else:
+            gsa, gsb, alpha = shard.sharded_global_scales(a, b, a_sharded=False, b_sharded=True)
+            (qa, sa), (qb, sb) = _lib.quant_nvfp4(a, gsa), _lib.quant_nvfp4(b, gsb)
+            st = (qa, qb, sa, sb, alpha)
+            if ev is not None:
+                ev[0].record(stream)
+            out = _lib.gemm(qa, qb, sa, sb, fmt=0, group_size=16, w_reduce=4, stage3_rounding=0,
+                            stage4_rounding=0, alpha=alpha, out_mode=0)
         if ev is not None:
             ev[1].record(stream)
         return st, out
@@ -483,11 +503,26 @@ def main() -> int:
     gemm_ms = sum(s.elapsed_time(e) for s, e in gemm_ev) / args.steps
     finite_frac = float(torch.isfinite(out).float().mean())
 
+    # ---- the assembled output: one all_gather of the column slices (timed on its own, not in value)
+    gather_ms = None
+    if world > 1:
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        shard.gather_columns(out, N)
+        torch.cuda.synchronize()
+        dist.barrier()
+        g0.record(stream)
+        full = shard.gather_columns(out, N)
+        g1.record(stream)
+        torch.cuda.synchronize()
+        gather_ms = g0.elapsed_time(g1)
+        assert full.shape == (M, N)
+        del full
+
     # ---- end to end: pinned host inputs -> device -> quant + emul -> host output, every step.  The
     # copies run on their own streams with two device input buffers, so step i's host->device copy
     # overlaps step i-1's compute and its device->host copy overlaps step i+1's (a serving pipeline).
     a_p, b_p = a_h.pin_memory(), b_h.pin_memory()
-    out_h = torch.empty((M, N), dtype=torch.float16).pin_memory()
+    out_h = torch.empty((M, n1 - n0), dtype=torch.float16).pin_memory()
     s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
     a_buf = [torch.empty_like(a_d), torch.empty_like(a_d)]
     b_buf = [torch.empty_like(b_d), torch.empty_like(b_d)]
@@ -533,19 +568,58 @@ def main() -> int:
     e2e_local = e0.elapsed_time(e1)
     clk.samples += clk_e2e.samples     # the clock record covers both timed regions
 
-    times = torch.tensor([ms_local, e2e_local, gemm_ms], dtype=torch.float64, device=dev)
+    # ---- several GPUs: also the earlier mode, an independent full case per rank (weak scaling)
+    weak_ms = None
+    if world > 1:
+        a_w, b_w = make_inputs(rank)
+        a_w, b_w = a_w.to(dev), b_w.to(dev)
+
+        def weak_step():
+            return emul_fn(quant_fn(a_w, b_w))
+
+        for _ in range(args.warmup):
+            weak_step()
+        torch.cuda.synchronize()
+        dist.barrier()
+        w0, w1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        w0.record(stream)
+        for _ in range(args.steps):
+            weak_step()
+        w1.record(stream)
+        torch.cuda.synchronize()
+        weak_ms = w0.elapsed_time(w1)
+        del a_w, b_w
+
+    times = torch.tensor([ms_local, e2e_local, gemm_ms, gather_ms or 0.0, weak_ms or 0.0], dtype=torch.float64,
+                         device=dev)
     if world > 1:
         dist.all_reduce(times, op=dist.ReduceOp.MAX)
-    ms_max, e2e_max, gemm_max = times.tolist()
+    ms_max, e2e_max, gemm_max, gather_max, weak_max = times.tolist()
 
     if rank == 0:
-        macs = M * N * K
-        value = world * macs * args.steps / (ms_max / 1e3)
-        e2e_v = world * macs * args.steps / (e2e_max / 1e3)
+        macs = M * N * K                       # the whole job: one GEMM per step, split over the ranks
+        macs_rank = M * (n1 - n0) * K          # rank 0's share, for the per-launch roofline
+        value = macs * args.steps / (ms_max / 1e3)
+        e2e_v = macs * args.steps / (e2e_max / 1e3)
         pk, pk_kind = peaks()
-        # stage 1 is M*N*K fp16 tensor-core MACs (2 flops each); emul_fn's launches are timed together
-        achieved = 2.0 * macs / (gemm_max / 1e3) / 1e12
-        peak = pk.get("bf16_tflops", 1590.0)
+        clk_s = clk.summary()
+        mhz = clk_s.get("sm_mhz") or clk_s.get("sm_max_mhz") or 1965
+        n_sm = torch.cuda.get_device_properties(dev).multi_processor_count
+        # floors of one rank's emul_fn: stage 1 on the tensor cores (2*M*n*K flops), the stage-4 chain
+        # on the FP64 pipe (one DADD + one DFMA per output and 64-wide K block: 2*M*n*K/64 operations,
+        # 64 per clock per SM, measured on this B200), and the compulsory bytes from HBM
+        tensor_ms = 2.0 * macs_rank / (pk.get("bf16_tflops", 1590.0) * 1e12) * 1e3
+        fp64_ops = 2.0 * macs_rank / 64
+        fp64_peak = 64.0 * n_sm * mhz * 1e6
+        fp64_ms = fp64_ops / fp64_peak * 1e3
+        nr = n1 - n0
+        hbm_bytes = M * K // 2 + nr * K // 2 + (-(-M // 128) * 128 + -(-nr // 128) * 128) * (K // 16) + 2 * M * nr
+        hbm_ms = hbm_bytes / (pk.get("hbm_gbs", 6650.0) * 1e9) * 1e3
+        floors = {"tensor": tensor_ms, "fp64": fp64_ms, "hbm": hbm_ms}
+        bound = max(floors, key=floors.get)    # the binding floor (FP64 at the benchmark shape)
+        t_s = gemm_max / 1e3
+        achieved = {"tensor": 2.0 * macs_rank / t_s / 1e12, "fp64": fp64_ops / t_s / 1e12, "hbm": hbm_bytes / t_s / 1e9}
+        peak_of = {"tensor": pk.get("bf16_tflops", 1590.0), "fp64": fp64_peak / 1e12, "hbm": pk.get("hbm_gbs", 6650.0)}
         cpu = None
         if not args.no_cpu_baseline and world == 1:
             try:
@@ -553,34 +627,35 @@ def main() -> int:
                 cpu = cpu_baseline(sc)
             except Exception as e:  # reported, not fatal
                 cpu = {"value": None, "error": f"{type(e).__name__}: {e}"}
-        # the other floor of this kernel: its stage-4 chain, one DADD + one DFMA per output and 64-wide K
-        # block on the CUDA cores (FP64 pipe: 64 results per clock per SM, measured on this B200 with a
-        # DADD-only microbenchmark), at the median SM clock sampled during the timed region
-        clk_s = clk.summary()
-        mhz = clk_s.get("sm_mhz") or clk_s.get("sm_max_mhz") or 1965
-        n_sm = torch.cuda.get_device_properties(dev).multi_processor_count
-        fp64_ops = 2.0 * macs / 64
-        fp64_floor_ms = fp64_ops / (64.0 * n_sm * mhz * 1e6) * 1e3
         line = {
             "metric": "emulated FP4 GEMM MAC/s at 8192^3" if (M, N, K) == (8192, 8192, 8192)
                       else f"emulated FP4 GEMM MAC/s at {M}x{N}x{K} (profiling size)",
             "value": value, "unit": "MAC/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "ms_per_step": ms_max / args.steps, "higher_is_better": True,
+            "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
             "dtype": "int32/f64", "data": "synthetic",
-            "config": {"workload": f"NVFP4 emulated GEMM M={M} N={N} K={K} per GPU, fp16 A/B |N(0,1)| with 1% outlier "
+            "config": {"workload": f"NVFP4 emulated GEMM M={M} N={N} K={K}, fp16 A/B |N(0,1)| with 1% outlier "
                                    "columns x100, quant_fn + emul_fn per step, fp16 out",
                        "M": M, "N": N, "K": K, "format": "nvfp4", "w_reduce": 4, "rounding": "RZ/RZ",
                        "l2": "inputs larger than L2 (fp16 A+B = 268 MB read per step)",
-                       "parallelism": f"independent case per GPU x{world}"},
-            "e2e": {"value": e2e_v, "unit": "MAC/s", "h2d_bytes_per_step": 2 * M * K * 2, "d2h_bytes_per_step": M * N * 2},
-            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                         "frac": achieved / peak, "traffic": ncu_traffic() if (M, N, K) == (8192, 8192, 8192) else None,
-                         "kernel": "emul_fn launches (pre-pass kernels + emul_gemm_tc_kernel), CUDA events",
-                         "kernel_ms": gemm_max, "work_per_launch": "2*M*N*K stage-1 tensor-core flops",
-                         "peak_kind": f"bf16 dense burst, {pk_kind}",
-                         "cuda_core": {"what": "stage-4 chain: DADD + DFMA per output and K block, FP64 pipe",
-                                       "fp64_ops": fp64_ops, "peak_ops_per_s": 64.0 * n_sm * mhz * 1e6,
-                                       "floor_ms": fp64_floor_ms, "frac": fp64_floor_ms / gemm_max}},
+                       "parallelism": "one GEMM per step" + (f", output columns split over {world} GPUs (B rows "
+                                      f"{n1 - n0} per GPU, all of A on each), global scale of B by one "
+                                      "all_reduce MAX of amax words" if world > 1 else "")},
+            "e2e": {"value": e2e_v, "unit": "MAC/s", "h2d_bytes_per_step": world * (M * K * 2) + N * K * 2,
+                    "d2h_bytes_per_step": M * N * 2},
+            "roofline": {"bound": bound, "achieved": achieved[bound], "peak": peak_of[bound],
+                         "unit": "GB/s" if bound == "hbm" else "TFLOP/s",
+                         "frac": achieved[bound] / peak_of[bound],
+                         "traffic": ncu_traffic() if (M, N, K) == (8192, 8192, 8192) and world == 1 else None,
+                         "kernel": "one rank's emul_fn launches (pre-pass kernels + emul_gemm_tc_kernel), CUDA events",
+                         "kernel_ms": gemm_max,
+                         "work_per_launch": f"M*n*K = {macs_rank} emulated MACs (n = this rank's columns): "
+                                            f"{2 * macs_rank} stage-1 tensor flops, {fp64_ops:.4g} FP64 stage-4 "
+                                            f"operations, {hbm_bytes} compulsory bytes",
+                         "floors_ms": floors,
+                         "peaks": {"fp64_ops_per_s": fp64_peak, "fp64_kind": "64/clk/SM measured with a DADD "
+                                   "microbenchmark, at the median SM clock sampled", "bf16_tflops": pk.get("bf16_tflops"),
+                                   "hbm_gbs": pk.get("hbm_gbs"), "kind": pk_kind}},
             # emul_fn returns fp16 like the reference emulator (nvfp_emulation.cpp:155); at this data
             # |C| is about 5e5 (82 outlier channels x 100 x 100), above fp16's 65504, so the returned
             # values saturate to inf there exactly as the reference's do -- the f32 accumulation before
@@ -589,6 +664,12 @@ def main() -> int:
             "gpu_launches": None if launches_per_step is None else launches_per_step * args.steps,
             "clocks": clk.summary(),
         }
+        if world > 1:
+            line["c_all_gather_ms"] = gather_max
+            line["value_with_all_gather"] = macs / ((ms_max / args.steps + gather_max) / 1e3)
+            line["independent_cases"] = {"value": world * macs * args.steps / (weak_max / 1e3), "unit": "MAC/s",
+                                         "scaling": "weak", "ms_per_step": weak_max / args.steps,
+                                         "what": "a separate seeded 8192^3 case on every GPU, quant_fn + emul_fn"}
         if cpu is not None:
             line["cpu_baseline"] = cpu
         print(json.dumps(line))
@@ -596,7 +677,6 @@ def main() -> int:
         dist.barrier()
         dist.destroy_process_group()
     return 0
-
 
 if __name__ == "__main__":
     raise SystemExit(main())
