@@ -27,7 +27,7 @@ ABI_VERSION = 1
 SYMBOLS = ("emu_abi_version", "emu_last_error", "emu_status_string", "emu_gemm", "emu_gemm_workspace_size", "emu_gemm_tc_workspace_size",
            "emu_gemm_ws", "emu_gemm_tc_path_offset", "emu_gemm_static", "emu_nvfp4_global_scales", "emu_nvfp4_amax",
            "emu_nvfp4_scales_from_amax", "emu_quant_nvfp4", "emu_quant_mxfp4",
-           "emu_gemm_model", "emu_gemm_compare", "emu_compare", "emu_dequant_fp4", "emu_device_status",
+           "emu_gemm_model", "emu_gemm_sweep", "emu_gemm_compare", "emu_compare", "emu_dequant_fp4", "emu_device_status",
            "emu_set_wait_limit", "emu_test_hold_first_ready")
 STATIC_SCRATCH_BYTES = 64 << 20   # EMU_STATIC_SCRATCH_BYTES
 
@@ -47,6 +47,11 @@ class EmuCompareStats(ctypes.Structure):
 class EmuAccumModel(ctypes.Structure):
     _fields_ = [("align3", ctypes.c_int32), ("align4", ctypes.c_int32), ("align_rounding", ctypes.c_int32),
                 ("order", ctypes.c_int32)]
+
+
+class EmuSweepModel(ctypes.Structure):
+    _fields_ = [("w_reduce", ctypes.c_int32), ("stage4_rounding", ctypes.c_int32), ("align3", ctypes.c_int32),
+                ("align4", ctypes.c_int32), ("align_rounding", ctypes.c_int32), ("order", ctypes.c_int32)]
 
 
 class EmuError(RuntimeError):
@@ -107,6 +112,9 @@ def load() -> ctypes.CDLL:
         L.emu_gemm_model.restype = i32
         L.emu_gemm_model.argtypes = [vp, vp, vp, vp, i64, i64, i64, i64, i64, i64, i64, vp,
                                      ctypes.POINTER(EmuGemmParams), ctypes.POINTER(EmuAccumModel), vp, vp]
+        L.emu_gemm_sweep.restype = i32
+        L.emu_gemm_sweep.argtypes = [vp, vp, vp, vp, i64, i64, i64, i64, i64, i64, i64, vp, i32, i32,
+                                     ctypes.POINTER(EmuSweepModel), i32, vp, i32, vp, vp]
         L.emu_gemm_compare.restype = i32
         L.emu_gemm_compare.argtypes = [vp, vp, vp, vp, i64, i64, i64, i64, i64, i64, i64, vp,
                                        ctypes.POINTER(EmuGemmParams), vp, vp, vp, vp, ctypes.c_size_t, vp]
@@ -433,3 +441,31 @@ def gemm_model(a_fp4: torch.Tensor, b_fp4: torch.Tensor, scale_a: torch.Tensor, 
                                   out.data_ptr(), _stream(dev))
     _check(status)
     return out.cpu() if on_cpu else out
+
+
+def gemm_sweep(a_fp4: torch.Tensor, b_fp4: torch.Tensor, scale_a: torch.Tensor, scale_b: torch.Tensor,
+               ref: torch.Tensor, models: list, *, fmt: int, stage3_rounding: int = EMU_RZ,
+               alpha: torch.Tensor | None = None) -> list[int]:
+    """Mismatch count of each accumulator model against `ref` (emu_gemm_sweep).  `models` holds
+    (w_reduce, stage4_rounding, align3, align4, align_rounding, order) tuples."""
+    L = load()
+    dev = _device_for(a_fp4, b_fp4, scale_a, scale_b, ref)
+    M, N, K = a_fp4.shape[0], b_fp4.shape[0], a_fp4.shape[1] * 2
+    a = _bytes2d(a_fp4, dev, "a_fp4")
+    b = _bytes2d(b_fp4, dev, "b_fp4")
+    sa = _bytes2d(scale_a, dev, "scale_a")
+    sb = _bytes2d(scale_b, dev, "scale_b")
+    r = ref.to(device=dev).contiguous()
+    if tuple(r.shape) != (M, N):
+        raise RuntimeError(f"ref must be [{M}, {N}], got {tuple(r.shape)}")
+    al = None if alpha is None else alpha.detach().reshape(1).to(device=dev, dtype=torch.float32).contiguous()
+    arr = (EmuSweepModel * max(1, len(models)))(*[EmuSweepModel(*m) for m in models])
+    counts = torch.empty(max(1, len(models)), dtype=torch.int64, device=dev)
+    with torch.cuda.device(dev):
+        st = L.emu_gemm_sweep(a.data_ptr(), b.data_ptr(), sa.data_ptr(), sb.data_ptr(), M, N, K, sa.shape[0],
+                              sa.shape[1], sb.shape[0], sb.shape[1], None if al is None else al.data_ptr(), fmt,
+                              stage3_rounding, arr, len(models), r.data_ptr(), _cmp_dtype(r), counts.data_ptr(),
+                              _stream(dev))
+    _check(st)
+    device_status(dev)   # reading the counts synchronises anyway
+    return [int(x) for x in counts[: len(models)].cpu()]

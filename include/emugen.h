@@ -199,6 +199,36 @@ EMU_API int64_t emu_set_wait_limit(int64_t cycles);
 EMU_API emu_status emu_test_hold_first_ready(int32_t enable);
 
 /*
+ * One model of an accumulator-model sweep: the block size and stage-4 rounding it runs with, and the
+ * emu_accum_model fields (all zero = the reference model at that block size).
+ */
+typedef struct emu_sweep_model {
+  int32_t w_reduce;         /* groups per stage-3 block: 1, 2, 4 or 8, a divisor of K / group size */
+  int32_t stage4_rounding;  /* EMU_RZ / EMU_RNE                                                   */
+  int32_t align3;           /* as emu_accum_model                                                 */
+  int32_t align4;
+  int32_t align_rounding;
+  int32_t order;
+} emu_sweep_model;
+
+/*
+ * Accumulator-model sweep: the emulated GEMM of (a_fp4, b_fp4) under each of n_models models, every
+ * result -- the f32 accumulator times alpha, rounded once to ref_dtype (EMU_DTYPE_F16 / BF16 / F32)
+ * -- compared element-wise with `ref` ([M][N], device) by gemm_compare's rule (equal, or NaN on both
+ * sides, gemm_compare/runner.py:20-55); mismatches[i] (device int64[n_models], overwritten) receives
+ * model i's mismatch count.  No output is written.  Stages 1-2 run once per group for all models of
+ * one block size.  Replaces the reference's one-emulation-per-candidate loops (search/w3.py:123-158,
+ * search/w4.py:60-90) for the models emu_gemm_model defines; bit for bit emu_gemm_model's results.
+ * format / stage3_rounding as in emu_gemm_params (stage3_rounding applies when K / group == w_reduce).
+ */
+EMU_API emu_status emu_gemm_sweep(const uint8_t* a_fp4, const uint8_t* b_fp4, const uint8_t* scale_a,
+                                  const uint8_t* scale_b, int64_t M, int64_t N, int64_t K, int64_t scale_a_rows,
+                                  int64_t scale_a_cols, int64_t scale_b_rows, int64_t scale_b_cols,
+                                  const float* alpha, int32_t format, int32_t stage3_rounding,
+                                  const emu_sweep_model* models, int32_t n_models, const void* ref,
+                                  int32_t ref_dtype, int64_t* mismatches, void* stream);
+
+/*
  * Bytes of the per-device static scratch behind emu_gemm_static (64 MiB).  The array belongs to the
  * library's device module: every device on which that module is loaded holds it (64 MiB + 1 KiB)
  * until the process exits, whether or not emu_gemm_static is called -- at library load under
