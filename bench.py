@@ -270,7 +270,8 @@ def run_workload(args) -> int:
     c2   MXFP4 4096^3, 100 seeded cases (50 ~N(0,1), 50 Student-t(3)), bf16 in and out: quant_fn + emul_fn
          per case (inputs drawn on the device from a seeded generator so the 100 draws take seconds);
     c4   NVFP4 decode shapes M in {1, 8, 32, 128} x (N, K) in {(4096, 4096), (14336, 4096), (4096, 14336),
-         (128256, 4096)}, B ~N(0, 0.02), A ~N(0, 1), fp16 out: emul_fn per shape vs its compulsory bytes;
+         (128256, 4096)}, B ~N(0, 0.02), A ~N(0, 1), fp16 out: emul_fn per shape vs its compulsory bytes
+         (--shape M,N,K: that one shape, timed over --steps launches after 3 untimed ones);
     c5   MXFP4 8192^3 ~N(0,1), bf16: the accumulator-model GEMM under 56 configurations (alignment width
          24..31 x {RZ, RNE} alignment rounding x accumulate size {32, 64, 128}, plus 8 summation orders),
          each compared on the device with the hardware FP4 GEMM (flashinfer) -- mismatch counts (the model's
@@ -345,16 +346,20 @@ def run_workload(args) -> int:
         from emugen_b200 import nvfp4_global_scales, quant_nvfp4
 
         rows = []
-        for (nn, kk) in [(4096, 4096), (14336, 4096), (4096, 14336), (128256, 4096)]:
+        grid = [((nn, kk), (1, 8, 32, 128)) for nn, kk in [(4096, 4096), (14336, 4096), (4096, 14336), (128256, 4096)]]
+        if args.shape:
+            mm, nn, kk = (int(x) for x in args.shape.split(","))
+            grid = [((nn, kk), (mm,))]
+        for (nn, kk), ms_ in grid:
             g = torch.Generator().manual_seed(SEED + nn + kk)
             bw = (torch.randn(nn, kk, generator=g) * 0.02).half().to(dev)
-            for mm in (1, 8, 32, 128):
+            for mm in ms_:
                 a = torch.randn(mm, kk, generator=g).half().to(dev)
                 gsa, gsb, alpha = nvfp4_global_scales(a, bw)
                 (qa, sa), (qb, sb) = quant_nvfp4(a, gsa), quant_nvfp4(bw, gsb)
                 kw = dict(fmt=0, group_size=16, w_reduce=4, stage3_rounding=0, stage4_rounding=0, alpha=alpha,
                           out_mode=0)
-                ms = timed(lambda: _lib.gemm(qa, qb, sa, sb, **kw), 20)
+                ms = timed(lambda: _lib.gemm(qa, qb, sa, sb, **kw), 20 if not args.shape else args.steps)
                 pad = lambda x, m: (x + m - 1) // m * m
                 byts = mm * kk // 2 + nn * kk // 2 + (pad(mm, 128) + pad(nn, 128)) * pad(kk // 16, 4) + 2 * mm * nn
                 rows.append({"M": mm, "N": nn, "K": kk, "us": ms * 1e3, "compulsory_MB": byts / 1e6,
@@ -418,6 +423,7 @@ def main() -> int:
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
+    ap.add_argument("--shape", default="", help="c4 only: one decode shape M,N,K instead of the grid")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--mnk", default=None, help="M,N,K (default 8192,8192,8192)")
     ap.add_argument("--workload", default="headline", choices=("headline", "c1", "c2", "c4", "c5"),
@@ -632,7 +638,7 @@ def main() -> int:
                       else f"emulated FP4 GEMM MAC/s at {M}x{N}x{K} (profiling size)",
             "value": value, "unit": "MAC/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": ms_max / args.steps, "higher_is_better": True,
-            "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
+            "scaling": "strong", "vs_baseline": None,
             "dtype": "int32/f64", "data": "synthetic",
             "config": {"workload": f"NVFP4 emulated GEMM M={M} N={N} K={K}, fp16 A/B |N(0,1)| with 1% outlier "
                                    "columns x100, quant_fn + emul_fn per step, fp16 out",

@@ -40,6 +40,12 @@ cudaError_t launch_gemm_sweep(const uint8_t* A, const uint8_t* B, const uint8_t*
                               int w_reduce, int r3, const SweepModel* models, const int* slots, int n,
                               const void* ref, int ref_dtype, unsigned long long* mismatches, cudaStream_t stream);
 
+// Decode shapes (M < 128) on the integer MMA, 16 output columns per warp (gemm_decode.cu).
+bool gemm_decode_supported(int fmt, int64_t M, int64_t N, int64_t K, const void* A, const void* B, const void* SB);
+cudaError_t launch_gemm_decode(const uint8_t* A, const uint8_t* B, const uint8_t* SA, const uint8_t* SB, int64_t M,
+                               int64_t N, int64_t K, int64_t sa_cols, int64_t sb_cols, const float* alpha,
+                               const GemmArgs& args, void* out, cudaStream_t stream);
+
 // Skinny problems (M < 128): block sums split over warps, stage-4 chains per output (gemm_skinny.cu).
 bool gemm_skinny_supported(int fmt, int w_reduce, int64_t M);
 cudaError_t launch_gemm_skinny(const uint8_t* A, const uint8_t* B, const uint8_t* SA, const uint8_t* SB, int64_t M,
