@@ -48,6 +48,8 @@ constexpr int DC_COLS = 16;                        // output columns per warp (t
 constexpr int DC_CTA_COLS = DC_COLS * DC_WARPS;    // 128
 constexpr int DC_WIN = 1024;                       // K elements of A per staged window
 constexpr int DC_CHUNK = 64;                       // packed bytes of one column per chunk (128 elements)
+constexpr int DC_SCS = 80;                         // bytes per column of a chunk's converted B scales (8 f64 + pad)
+constexpr int DC_XBUF = DC_COLS * DC_CHUNK + DC_COLS * DC_SCS;   // one exchange buffer of a warp
 
 template <int FMT> struct DcFmt {
   static constexpr int GS = FMT == EMU_FMT_NVFP4 ? 16 : 32;     // elements per scale group
@@ -146,6 +148,9 @@ __device__ __forceinline__ uint4 lds_v4(uint32_t a) {
   asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
   return v;
 }
+__device__ __forceinline__ void sts_f64x2(uint32_t a, double x, double y) {
+  asm volatile("st.shared.v2.f64 [%0], {%1, %2};" ::"r"(a), "d"(x), "d"(y) : "memory");
+}
 __device__ __forceinline__ void sts_v4(uint32_t a, uint4 v) {
   asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w) : "memory");
 }
@@ -163,11 +168,13 @@ __device__ __forceinline__ int64_t swz_row_base(int64_t r, int64_t cols_pad) {
 //   asc   [NT] 2 KB                 A scales: NVFP4 int32 sa * 2^9 [group / 2][row][group % 2],
 //                                   MXFP4 f64 2^(ua - 129) [group][row]
 //   flg   [NT][16]                  per group quad, bit i: some |p4| of the (tile, group 4 quad + i) may reach 2048
-//   xch   [8 warps][2][16 cols][64] B exchange buffers
+//   xch   [8 warps]                 B exchange buffer: [16 cols][64] packed bytes, then [16 cols][80 B] the
+//                                   chunk's column scales as f64 (8 groups; the pad spreads the columns over the
+//                                   banks, so the quad-broadcast 16-byte reads of 8 columns are conflict-free)
 template <int NT>
 struct DcSmem {
   static constexpr size_t LUT = 0, AFR = 2048, ASC = AFR + (size_t)NT * 16384, FLG = ASC + (size_t)NT * 2048,
-                          XCH = FLG + (size_t)NT * 64, BYTES = XCH + (size_t)DC_WARPS * 2 * DC_COLS * DC_CHUNK;
+                          XCH = FLG + (size_t)NT * 64, BYTES = XCH + (size_t)DC_WARPS * DC_XBUF;
 };
 
 // WRC: the block size (w_reduce) when it is fixed at compile time (it divides the chunk's groups, so
@@ -218,23 +225,23 @@ emul_gemm_decode_kernel(const uint8_t* __restrict__ A, const uint8_t* __restrict
   const uint8_t* s1p = SB + swz_row_base(ok1 ? col1 : 0, sb_cols);
   const uint32_t sm0 = smem_addr(dc_smem);
   const uint32_t lut_a = sm0 + L::LUT, afr_a = sm0 + L::AFR, asc_a = sm0 + L::ASC, flg_a = sm0 + L::FLG;
-  const uint32_t xch_a = sm0 + L::XCH + warp * (2 * DC_COLS * DC_CHUNK);
+  const uint32_t xch_a = sm0 + L::XCH + warp * DC_XBUF;
   const int sw = (c >> 1) & 3;   // exchange swizzle of columns c and c + 8
 
   // chunk loads: 16 bytes per column and lane, the chunk's scale words (NVFP4 two, MXFP4 one per column)
   const int64_t nchunks = (kbytes + DC_CHUNK - 1) / DC_CHUNK;
-  constexpr int SWN = NV ? 2 : 1;
-  auto load_chunk = [&](int64_t k, uint4& w0, uint4& w1, uint32_t (&s0)[SWN], uint32_t (&s1)[SWN]) {
+  constexpr int SWN = NV ? 2 : 1;                      // scale words per column and chunk
+  // the quad's four lanes share the scales of columns c and c + 8: lane q loads and converts one word of
+  // them, column q / 2, NVFP4 word q % 2 (groups 4 (q % 2) ..), MXFP4 bytes 2 (q % 2) .. of the one word
+  const bool okq = (q >> 1) ? ok1 : ok0;
+  const uint8_t* sqp = (q >> 1) ? s1p : s0p;
+  const int hq = NV ? (q & 1) : 0;
+  auto load_chunk = [&](int64_t k, uint4& w0, uint4& w1, uint32_t& swd) {
     const bool in = k * DC_CHUNK + 16 * q < kbytes;
     w0 = (ok0 && in) ? __ldg(reinterpret_cast<const uint4*>(b0p + k * DC_CHUNK)) : make_uint4(0u, 0u, 0u, 0u);
     w1 = (ok1 && in) ? __ldg(reinterpret_cast<const uint4*>(b1p + k * DC_CHUNK)) : make_uint4(0u, 0u, 0u, 0u);
-#pragma unroll
-    for (int h = 0; h < SWN; ++h) {
-      const int64_t g4 = k * SWN + h;                // scale word: groups 4 g4 .. 4 g4 + 3
-      const bool gin = 4 * g4 < G;
-      s0[h] = (ok0 && gin) ? __ldg(reinterpret_cast<const uint32_t*>(s0p + g4 * 512)) : 0u;
-      s1[h] = (ok1 && gin) ? __ldg(reinterpret_cast<const uint32_t*>(s1p + g4 * 512)) : 0u;
-    }
+    const int64_t g4 = k * SWN + hq;                   // scale word: groups 4 g4 .. 4 g4 + 3
+    swd = (okq && 4 * g4 < G) ? __ldg(reinterpret_cast<const uint32_t*>(sqp + g4 * 512)) : 0u;
   };
 
   double S[NT][4];
@@ -246,10 +253,9 @@ emul_gemm_decode_kernel(const uint8_t* __restrict__ A, const uint8_t* __restrict
   int gi = 0;           // groups of the current block so far (block size read from args)
 
   uint4 nw0, nw1;
-  uint32_t ns0[SWN], ns1[SWN];
-  load_chunk(0, nw0, nw1, ns0, ns1);
+  uint32_t nsw;
+  load_chunk(0, nw0, nw1, nsw);
   int64_t k = 0;        // next chunk to process
-  int xb = 0;           // exchange buffer
 
   for (int64_t e0 = 0; e0 < K; e0 += DC_WIN) {
     const int welems = (int)std::min<int64_t>(DC_WIN, K - e0);
@@ -316,13 +322,24 @@ emul_gemm_decode_kernel(const uint8_t* __restrict__ A, const uint8_t* __restrict
     const int64_t kend = (e0 + welems + 127) / 128;   // chunks of 128 elements; a 64-element tail is a half chunk
     for (; k < kend; ++k) {
       const uint4 w0 = nw0, w1 = nw1;
-      uint32_t s0[SWN], s1[SWN];
-#pragma unroll
-      for (int h = 0; h < SWN; ++h) s0[h] = ns0[h], s1[h] = ns1[h];
-      if (k + 1 < nchunks) load_chunk(k + 1, nw0, nw1, ns0, ns1);
+      const uint32_t sw_own = nsw;
+      if (k + 1 < nchunks) load_chunk(k + 1, nw0, nw1, nsw);
       // regroup: word p' = unit p' of the first 8 bytes | unit p' of the second 8 bytes << 16
       // (NVFP4: groups 2q, 2q+1; MXFP4: units p' and p' + 4 of group q); slot q ^ swizzle of the column
-      const uint32_t xbuf = xch_a + xb * (DC_COLS * DC_CHUNK);
+      const uint32_t xbuf = xch_a, scb = xbuf + DC_COLS * DC_CHUNK;
+      __syncwarp();   // every lane has read the previous chunk's exchange buffer
+      {   // this lane's scale word as f64 (table lookups), into [column][group]
+        const uint32_t cc = c + 8 * (q >> 1);
+        if constexpr (NV) {
+          const uint32_t dst = scb + cc * DC_SCS + hq * 32;
+          sts_f64x2(dst, lds_f64(lut_a + (sw_own & 0xFFu) * 8), lds_f64(lut_a + ((sw_own >> 8) & 0xFFu) * 8));
+          sts_f64x2(dst + 16, lds_f64(lut_a + ((sw_own >> 16) & 0xFFu) * 8), lds_f64(lut_a + (sw_own >> 24) * 8));
+        } else {
+          const uint32_t w = sw_own >> (16 * (q & 1));
+          sts_f64x2(scb + cc * DC_SCS + (q & 1) * 16, lds_f64(lut_a + (w & 0xFFu) * 8),
+                    lds_f64(lut_a + ((w >> 8) & 0xFFu) * 8));
+        }
+      }
       sts_v4(xbuf + (c * 4 + (q ^ sw)) * 16, make_uint4(prmt(w0.x, w0.z, 0x5410u), prmt(w0.x, w0.z, 0x7632u),
                                                         prmt(w0.y, w0.w, 0x5410u), prmt(w0.y, w0.w, 0x7632u)));
       sts_v4(xbuf + ((c + 8) * 4 + (q ^ sw)) * 16, make_uint4(prmt(w1.x, w1.z, 0x5410u), prmt(w1.x, w1.z, 0x7632u),
@@ -334,7 +351,6 @@ emul_gemm_decode_kernel(const uint8_t* __restrict__ A, const uint8_t* __restrict
         R0[m] = lds_u32(xbuf + ((c * 4 + (m ^ sw)) * 4 + q) * 4);
         R1[m] = lds_u32(xbuf + (((c + 8) * 4 + (m ^ sw)) * 4 + q) * 4);
       }
-      xb ^= 1;
 
       const int gwc = (int)(k * CG - e0 / GS);        // window group of the chunk's first group (a multiple of CG)
       uint32_t fl[NT];                                // stage-1 rounding flags of the chunk's groups, a bit each
@@ -348,6 +364,7 @@ emul_gemm_decode_kernel(const uint8_t* __restrict__ A, const uint8_t* __restrict
         }
       }
       const int jn = (int)std::min<int64_t>(CG, G - k * CG);   // groups of this chunk (a half chunk at the end)
+      double2 sbp0, sbp1;                             // column scales of two groups, columns c and c + 8
       uint4 apair[NT];                                // NVFP4: A and -A of two groups
       int4 spair[NT];                                 // NVFP4: sa of rows 2q, 2q+1 for two groups
 #pragma unroll
@@ -364,8 +381,11 @@ emul_gemm_decode_kernel(const uint8_t* __restrict__ A, const uint8_t* __restrict
           P[0] = pos4(R0[j]), P[1] = pos4(R1[j]), P[2] = pos4(R0[j] >> 16), P[3] = pos4(R1[j] >> 16);
           Q[0] = neg4(f0), Q[1] = neg4(f1), Q[2] = neg4(f0 >> 16), Q[3] = neg4(f1 >> 16);
         }
-        const double sb0 = lds_f64(lut_a + ((s0[j >> 2] >> (8 * (j & 3))) & 0xFFu) * 8);
-        const double sb1 = lds_f64(lut_a + ((s1[j >> 2] >> (8 * (j & 3))) & 0xFFu) * 8);
+        if ((j & 1) == 0) {   // the column scales of groups j, j + 1
+          sbp0 = lds_f64x2(scb + c * DC_SCS + j * 8);
+          sbp1 = lds_f64x2(scb + (c + 8) * DC_SCS + j * 8);
+        }
+        const double sb0 = (j & 1) ? sbp0.y : sbp0.x, sb1 = (j & 1) ? sbp1.y : sbp1.x;
         const bool first = WRC ? (j % (WRC ? WRC : 1)) == 0 : gi == 0;
 #pragma unroll
         for (int t = 0; t < NT; ++t) {
