@@ -364,13 +364,16 @@ emul_gemm_decode_kernel(const uint8_t* __restrict__ A, const uint8_t* __restrict
         }
       }
       const int jn = (int)std::min<int64_t>(CG, G - k * CG);   // groups of this chunk (a half chunk at the end)
+      // chunk bases of the A fragments and scales: a group's address is base + a compile-time offset
+      const uint32_t afr_c = afr_a + ((NV ? gwc >> 1 : gwc) * 32 + lane) * 16;
+      const uint32_t asc_c = asc_a + (NV ? ((gwc >> 1) * 16 + 4 * q) * 4 : (gwc * 8 + 2 * q) * 8);
+      const uint32_t scb0 = scb + c * DC_SCS, scb1 = scb + (c + 8) * DC_SCS;
       double2 sbp0, sbp1;                             // column scales of two groups, columns c and c + 8
       uint4 apair[NT];                                // NVFP4: A and -A of two groups
       int4 spair[NT];                                 // NVFP4: sa of rows 2q, 2q+1 for two groups
 #pragma unroll
       for (int j = 0; j < CG; ++j) {
         if (j >= jn) break;
-        const int gw = gwc + j;
         uint32_t P[4], Q[4];                          // B operand: positive / negative magnitudes
         if constexpr (NV) {
           const uint32_t x0 = R0[j >> 1] >> (16 * (j & 1)), x1 = R1[j >> 1] >> (16 * (j & 1));
@@ -382,8 +385,8 @@ emul_gemm_decode_kernel(const uint8_t* __restrict__ A, const uint8_t* __restrict
           Q[0] = neg4(f0), Q[1] = neg4(f1), Q[2] = neg4(f0 >> 16), Q[3] = neg4(f1 >> 16);
         }
         if ((j & 1) == 0) {   // the column scales of groups j, j + 1
-          sbp0 = lds_f64x2(scb + c * DC_SCS + j * 8);
-          sbp1 = lds_f64x2(scb + (c + 8) * DC_SCS + j * 8);
+          sbp0 = lds_f64x2(scb0 + j * 8);
+          sbp1 = lds_f64x2(scb1 + j * 8);
         }
         const double sb0 = (j & 1) ? sbp0.y : sbp0.x, sb1 = (j & 1) ? sbp1.y : sbp1.x;
         const bool first = WRC ? (j % (WRC ? WRC : 1)) == 0 : gi == 0;
@@ -392,15 +395,15 @@ emul_gemm_decode_kernel(const uint8_t* __restrict__ A, const uint8_t* __restrict
           uint32_t bp[2], bn[2];
           if constexpr (NV) {
             if ((j & 1) == 0) {
-              apair[t] = lds_v4(afr_a + ((t * 32 + (gw >> 1)) * 32 + lane) * 16);
-              const uint4 sv = lds_v4(asc_a + ((t * 32 + (gw >> 1)) * 16 + 4 * q) * 4);
+              apair[t] = lds_v4(afr_c + (t * 32 + (j >> 1)) * 32 * 16);
+              const uint4 sv = lds_v4(asc_c + (t * 32 + (j >> 1)) * 16 * 4);
               spair[t] = make_int4((int)sv.x, (int)sv.y, (int)sv.z, (int)sv.w);
             }
             bp[0] = (j & 1) ? apair[t].z : apair[t].x;
             bn[0] = (j & 1) ? apair[t].w : apair[t].y;
             bp[1] = bn[1] = 0u;
           } else {
-            const uint4 av = lds_v4(afr_a + ((t * 32 + gw) * 32 + lane) * 16);
+            const uint4 av = lds_v4(afr_c + (t * 32 + j) * 32 * 16);
             bp[0] = av.x, bp[1] = av.y, bn[0] = av.z, bn[1] = av.w;
           }
           int d[4];
@@ -419,7 +422,7 @@ emul_gemm_decode_kernel(const uint8_t* __restrict__ A, const uint8_t* __restrict
             S[t][2] = __fma_rn(flipped_i2d((uint32_t)d[2] * sa0 + 0x80000000u), sb1, first ? 0.0 : S[t][2]);
             S[t][3] = __fma_rn(flipped_i2d((uint32_t)d[3] * sa1 + 0x80000000u), sb1, first ? 0.0 : S[t][3]);
           } else {
-            const double2 sa = lds_f64x2(asc_a + ((t * 32 + gw) * 8 + 2 * q) * 8);
+            const double2 sa = lds_f64x2(asc_c + (t * 32 + j) * 8 * 8);
             S[t][0] = __fma_rn(flipped_i2d((uint32_t)d[0] + 0x80000000u), __dmul_rn(sa.x, sb0), first ? 0.0 : S[t][0]);
             S[t][1] = __fma_rn(flipped_i2d((uint32_t)d[1] + 0x80000000u), __dmul_rn(sa.y, sb0), first ? 0.0 : S[t][1]);
             S[t][2] = __fma_rn(flipped_i2d((uint32_t)d[2] + 0x80000000u), __dmul_rn(sa.x, sb1), first ? 0.0 : S[t][2]);
