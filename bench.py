@@ -277,7 +277,7 @@ def run_workload(args) -> int:
          each compared on the device with the hardware FP4 GEMM (flashinfer) -- mismatch counts (the model's
          f32 result rounded once to bf16, as the hardware's epilogue rounds).  Under torchrun the
          configurations are split over the ranks (emugen_b200.sweep.run_sweep_sharded: one broadcast of
-         the case, one all_reduce of the counts); time = max over ranks."""
+         the case, one all_reduce of the counts); time = max over ranks.  --mnk S,S,S: an S^3 case instead."""
     import torch
 
     from emugen_b200 import _lib
@@ -375,7 +375,7 @@ def run_workload(args) -> int:
             from datetime import timedelta
 
             dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
-        S = 8192
+        S = int(args.mnk.split(",")[0]) if args.mnk else 8192   # square problem; --mnk: a smaller one
         case, real, versus = None, None, None
         if rank == 0:
             g = torch.Generator(device=dev).manual_seed(SEED)
@@ -409,8 +409,8 @@ def run_workload(args) -> int:
             ms = float(t.item())
             dist.destroy_process_group()
         if rank == 0:
-            print(json.dumps({"workload": "c5 MXFP4 8192^3 accumulator-model sweep, %d configs on %d GPU(s)"
-                                          % (len(cfgs), world),
+            print(json.dumps({"workload": "c5 MXFP4 %d^3 accumulator-model sweep, %d configs on %d GPU(s)"
+                                          % (S, len(cfgs), world),
                               "versus": versus, "ms_total": ms, "ms_per_config": ms / len(cfgs) * world,
                               "MAC_per_s": len(cfgs) * S ** 3 / (ms / 1e3), "mismatches_min": min(mism),
                               "mismatches_max": max(mism), "mismatches": mism}))
