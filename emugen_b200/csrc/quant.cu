@@ -11,6 +11,12 @@
 //   q        = cvt.rn.satfinite.e2m1x2(x * outScale), low nibble = even element
 // where rcp is the hardware approximate reciprocal rcp.approx.ftz.f32 and outScale is 0 when
 // vecMax is 0.  The same PTX instructions are issued here so the bytes match bit for bit.
+// flashinfer builds those kernels with fast math, so f32 subnormals are flushed to (signed) zero
+// in its comparisons, products and exp2; this library is built without (the emulation kernels need
+// subnormals), so the flushes that change a byte are written out (ftz() below): the block maximum
+// and its product with rcp(6) (a bf16 block of subnormals: outScale 0, signed-zero codes), bf16
+// input elements before scaling, and MXFP4's outScale 2^(127 - SF), subnormal for SF >= 254 (a block
+// holding an infinity: outScale 0, so inf * 0 = NaN -> code 0x7 as flashinfer writes).
 // Layout: one thread per 16 input elements (32 bytes, two 16-byte loads); for MXFP4 two adjacent
 // lanes share a scale and combine their maxima with one shuffle.
 #include <cuda_bf16.h>
@@ -63,9 +69,12 @@ template <> struct Vec2<__nv_bfloat16> {
 
 // 2^(127 - e) as f32 bits for e in [1, 255] (exact, subnormal for e >= 254).
 __device__ __forceinline__ float pow2_127_minus(uint32_t e) {
-  if (e >= 254u) return __uint_as_float(0x00400000u >> (e - 254u));
+  if (e >= 254u) return 0.0f;   // 2^-127 and below: subnormal, flushed as in flashinfer's build
   return __uint_as_float((254u - e) << 23);
 }
+
+// f32 subnormal -> signed zero (fast-math flush-to-zero); NaN and inf pass
+__device__ __forceinline__ float ftz(float x) { return fabsf(x) < 1.17549435e-38f ? copysignf(0.0f, x) : x; }
 
 template <typename T, int SF_VEC>
 __global__ void __launch_bounds__(256)
@@ -103,18 +112,18 @@ quant_fp4_kernel(const T* __restrict__ x, int64_t M, int64_t K, const float* __r
         uint32_t ob = __shfl_xor_sync(0xFFFFFFFFu, lb, 1);
         local = __hmax2(*reinterpret_cast<V2*>(&ob), local);
       }
-      float vecMax = (float)((local.x > local.y) ? local.x : local.y);
+      float vecMax = ftz((float)((local.x > local.y) ? local.x : local.y));
 
       uint8_t sfbyte;
       float outScale;
       if (SF_VEC == 16) {
-        float sfv = gs * (vecMax * rcp_approx_ftz(6.0f));
+        float sfv = ftz(gs * ftz(vecMax * rcp_approx_ftz(6.0f)));
         __nv_fp8_e4m3 t = __nv_fp8_e4m3(sfv);
         sfbyte = t.__x;
         sfv = static_cast<float>(t);
         outScale = vecMax != 0.0f ? rcp_approx_ftz(sfv * rcp_approx_ftz(gs)) : 0.0f;
       } else {
-        vecMax = vecMax * rcp_approx_ftz(6.0f);
+        vecMax = ftz(vecMax * rcp_approx_ftz(6.0f));
         sfbyte = __nv_cvt_float_to_e8m0(vecMax, __NV_SATFINITE, cudaRoundPosInf);
         outScale = vecMax != 0.0f ? (sfbyte == 0 ? 1.0f : pow2_127_minus(sfbyte)) : 0.0f;
       }
@@ -124,6 +133,7 @@ quant_fp4_kernel(const T* __restrict__ x, int64_t M, int64_t K, const float* __r
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           float2 p = Vec2<T>::to_f2(e[i]);
+          if constexpr (!std::is_same<T, __half>::value) p = make_float2(ftz(p.x), ftz(p.y));   // fp16 has none
           f[2 * i] = __fmul_rn(p.x, outScale);
           f[2 * i + 1] = __fmul_rn(p.y, outScale);
         }

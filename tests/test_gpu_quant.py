@@ -137,3 +137,60 @@ def test_global_scales_vector_and_tail_paths(dtype):
     z[100] = float("nan")
     g, _, _ = nvfp4_global_scales(z, z)
     assert g.item() == float(want(z.cpu())) == 2688.0       # NaN > 0 is false: the reference falls back to 1.0
+
+
+def _parity(fi, x, gs):
+    from emugen_b200 import quant_mxfp4, quant_nvfp4
+
+    q_ref, sf_ref = fi.fp4_quantize(x, gs, 16, False, True)
+    q, sf = quant_nvfp4(x, gs)
+    nv = (int((q.cpu() != q_ref.view(torch.uint8).cpu()).sum()),
+          int((sf.cpu().reshape(-1) != sf_ref.view(torch.uint8).cpu().reshape(-1)).sum()))
+    q_ref, sf_ref = fi.mxfp4_quantize(x)
+    q, sf = quant_mxfp4(x)
+    mx = (int((q.cpu() != q_ref.view(torch.uint8).cpu()).sum()),
+          int((sf.cpu().reshape(-1) != sf_ref.view(torch.uint8).cpu().reshape(-1)).sum()))
+    return nv, mx
+
+
+@pytest.mark.parametrize("recipe", ["benchmark_outlier_columns_fp16", "student_t3_bf16"])
+def test_quant_bit_parity_on_benchmark_data(recipe):
+    """The benchmark's data recipes: |N(0,1)| fp16 with 1% of K columns x100 (NVFP4 8192^3 case; 1024
+    rows of it), and Student-t(3) bf16 (the MXFP4 suite's second half)."""
+    fi = _flashinfer_fp4_quantize()
+    from emugen_b200 import nvfp4_global_scales
+
+    g = torch.Generator().manual_seed(7)
+    if recipe.startswith("benchmark"):
+        x = torch.randn(1024, 8192, generator=g).abs_()
+        x[:, torch.randperm(8192, generator=g)[:82]] *= 100.0
+        x = x.half()
+    else:
+        z = torch.randn(1024, 4096, generator=g)
+        c = sum(torch.randn(1024, 4096, generator=g) ** 2 for _ in range(3))
+        x = (z / torch.sqrt(c / 3.0)).bfloat16()
+    x = x.cuda()
+    gs, _, _ = nvfp4_global_scales(x, x)
+    assert _parity(fi, x, gs) == ((0, 0), (0, 0))
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_quant_bit_parity_on_special_values(dtype):
+    """All-zero blocks, subnormal inputs, +-inf and NaN inside otherwise normal blocks, quantised with a
+    fixed global scale (the global scale of such operands has its own test above)."""
+    fi = _flashinfer_fp4_quantize()
+
+    g = torch.Generator().manual_seed(11)
+    x = torch.randn(256, 1024, generator=g)
+    x[0:8, :] = 0.0                                    # whole rows of zero blocks
+    x[8:16, 0:64] = 0.0                                # zero blocks inside a row
+    tiny = torch.finfo(dtype).tiny
+    x[16:32, :] = torch.randn(16, 1024, generator=g) * tiny * 0.25   # subnormal inputs
+    x[32, 5] = float("inf")
+    x[33, 100] = float("-inf")
+    x[34, 300] = float("nan")
+    x[35, 17:19] = float("nan")
+    x = x.to(dtype).cuda()
+    gs = torch.tensor([448.0 * 6.0 / 4.0], device="cuda")
+    nv, mx = _parity(fi, x, gs)
+    assert nv == (0, 0) and mx == (0, 0), (nv, mx)
