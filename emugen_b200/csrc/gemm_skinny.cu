@@ -369,6 +369,8 @@ bool gemm_skinny_supported(int fmt, int w_reduce, int64_t M) {
 cudaError_t launch_gemm_skinny(const uint8_t* A, const uint8_t* B, const uint8_t* SA, const uint8_t* SB, int64_t M,
                                int64_t N, int64_t K, int64_t sa_cols, int64_t sb_cols, const float* alpha,
                                const GemmArgs& args, void* out, cudaStream_t stream) {
+  if (gemm_gemv_supported(args.format, M, N, K, A, B, SB))
+    return launch_gemm_gemv(A, B, SA, SB, N, K, sa_cols, sb_cols, alpha, args, out, stream);
   if (gemm_decode_supported(args.format, M, N, K, A, B, SB))
     return launch_gemm_decode(A, B, SA, SB, M, N, K, sa_cols, sb_cols, alpha, args, out, stream);
   if (M == 1) return launch_rows<1>(A, B, SA, SB, M, N, K, sa_cols, sb_cols, alpha, args, out, stream);

@@ -46,6 +46,12 @@ cudaError_t launch_gemm_decode(const uint8_t* A, const uint8_t* B, const uint8_t
                                int64_t N, int64_t K, int64_t sa_cols, int64_t sb_cols, const float* alpha,
                                const GemmArgs& args, void* out, cudaStream_t stream);
 
+// One row of A on the CUDA cores, one output column per thread (gemm_decode.cu).
+bool gemm_gemv_supported(int fmt, int64_t M, int64_t N, int64_t K, const void* A, const void* B, const void* SB);
+cudaError_t launch_gemm_gemv(const uint8_t* A, const uint8_t* B, const uint8_t* SA, const uint8_t* SB, int64_t N,
+                             int64_t K, int64_t sa_cols, int64_t sb_cols, const float* alpha, const GemmArgs& args,
+                             void* out, cudaStream_t stream);
+
 // Skinny problems (M < 128): block sums split over warps, stage-4 chains per output (gemm_skinny.cu).
 bool gemm_skinny_supported(int fmt, int w_reduce, int64_t M);
 cudaError_t launch_gemm_skinny(const uint8_t* A, const uint8_t* B, const uint8_t* SA, const uint8_t* SB, int64_t M,

@@ -1,8 +1,8 @@
-"""GPU parity of the decode kernel (gemm_decode.cu: 2 <= M < 128 rows of A, N >= 8192 columns, stage 1 on
-the integer MMA), bit for bit: sampled columns (the first, the ragged last tile, a random set) against the
-C oracle, and every output against the skinny kernel on the same data -- the scales of B passed at an odd
-address, which the decode kernel declines (it reads them a word at a time) and the skinny kernel reads
-byte by byte."""
+"""GPU parity of the decode-shape kernels of gemm_decode.cu -- the decode kernel (2 <= M < 128 rows of A,
+N >= 8192 columns, stage 1 on the integer MMA) and the one-row kernel (M = 1, N >= 32768) -- bit for bit:
+sampled columns (the first, the ragged last tile, a random set) against the C oracle, and every output
+against the skinny kernels on the same data -- the scales of B passed at an odd address, which both
+kernels decline (they read them a word at a time) and the skinny kernels read byte by byte."""
 import zlib
 
 import numpy as np
@@ -29,6 +29,14 @@ CASES = [
     ("mxfp", "subnormal_acc", 17, 8192, 1024, 1, 1, 1, 0),
     ("mxfp", "flt_max", 7, 8192, 128, 2, 0, 0, 2),
     ("mxfp", "fp16_round", 12, 8320, 2112, 3, 0, 0, 1),     # w_reduce 3 (run time), 66 groups
+    # one row of A (emul_gemm_gemv_kernel): 4096-element windows, several and partial, ragged column tiles
+    ("nvfp", "normal", 1, 32808, 1024, 4, 0, 0, 0),
+    ("nvfp", "raw_nan_scales", 1, 32768, 9216, 4, 1, 1, 1),  # three windows; NaN scale codes in A and B
+    ("nvfp", "fp16_round", 1, 32768, 4160, 1, 0, 1, 2),      # flagged groups; a 64-element last window
+    ("nvfp", "huge_scales", 1, 33000, 5120, 16, 1, 0, 0),    # block size 16 (run time)
+    ("mxfp", "raw_scales_full", 1, 32768, 8256, 2, 0, 1, 2), # UE8M0 0 and 255 (inf)
+    ("mxfp", "subnormal_acc", 1, 32900, 2048, 1, 1, 1, 0),
+    ("mxfp", "normal", 1, 32768, 1024, 2, 0, 0, 1),
 ]
 IDS = [f"{c[0]}-{c[1]}-{c[2]}x{c[3]}x{c[4]}-wr{c[5]}" for c in CASES]
 
@@ -86,7 +94,7 @@ def test_decode_vs_oracle_and_skinny(kind, data, M, N, K, wr, r3, r4, out):
     kw = dict(fmt=fmt, group_size=gs, w_reduce=wr, stage3_rounding=r3, stage4_rounding=r4,
               alpha=None if al is None else torch.tensor([al], device="cuda"), out_mode=out)
     assert tsb.data_ptr() % 4 == 0
-    got = _lib.gemm(ta, tb, tsa, tsb, path="simt", **kw)       # M < 128, no workspace: the decode kernel
+    got = _lib.gemm(ta, tb, tsa, tsb, path="simt", **kw)       # M < 128, no workspace: the decode / one-row kernel
 
     # the same scales at an odd address: the skinny kernel
     buf = torch.zeros(tsb.numel() + 1, dtype=torch.uint8, device="cuda")
