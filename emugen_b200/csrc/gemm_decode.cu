@@ -562,16 +562,18 @@ emul_gemm_gemv_kernel(const uint8_t* __restrict__ A, const uint8_t* __restrict__
   const uint8_t* sp = SB + swz_row_base(ok ? col : 0, sb_cols);
   const int64_t nchunks = (kbytes + DC_CHUNK - 1) / DC_CHUNK;
   constexpr int SWN = NV ? 2 : 1;                  // scale words per chunk
+  // chunk k: bytes 64k .. of the column (32-bit offsets: a column holds under 2^31 bytes), the scale words of
+  // groups 4 (SWN k + h) ..; a 64-element tail chunk holds two 16-byte pieces
   auto load_chunk = [&](int64_t k, uint4 (&w)[4], uint32_t (&s)[SWN]) {
+    const int rem = ok ? (int)(kbytes - k * DC_CHUNK) : 0;   // bytes of the column from this chunk on
+    const uint8_t* cp = bp + k * DC_CHUNK;
 #pragma unroll
     for (int i = 0; i < 4; ++i)
-      w[i] = (ok && k * DC_CHUNK + 16 * i < kbytes) ? __ldg(reinterpret_cast<const uint4*>(bp + k * DC_CHUNK + 16 * i))
-                                                     : make_uint4(0u, 0u, 0u, 0u);
+      w[i] = 16 * i < rem ? __ldg(reinterpret_cast<const uint4*>(cp + 16 * i)) : make_uint4(0u, 0u, 0u, 0u);
+    const uint8_t* scp = sp + k * SWN * 512;
 #pragma unroll
-    for (int h = 0; h < SWN; ++h) {
-      const int64_t g4 = k * SWN + h;
-      s[h] = (ok && 4 * g4 < G) ? __ldg(reinterpret_cast<const uint32_t*>(sp + g4 * 512)) : 0u;
-    }
+    for (int h = 0; h < SWN; ++h)
+      s[h] = 32 * h < rem ? __ldg(reinterpret_cast<const uint32_t*>(scp + h * 512)) : 0u;   // word h: bytes 32h .. of the chunk
   };
 
   using SType = typename std::conditional<NV, long long, double>::type;
