@@ -9,10 +9,11 @@ data, drawn on the CPU and moved to the GPU.  One step = the public path a calle
 ``value`` is M*N*K per step with inputs resident in HBM; ``e2e`` adds, every step, the host->device
 copy of A, B from pinned memory and the device->host copy of the output, on copy streams that
 overlap the neighbouring steps' compute (double-buffered device inputs).  Multi-GPU (torchrun, one
-process per GPU): the same single GEMM per step, split by output columns (strong scaling) -- rank r
-holds all of A and its rows of B, takes the global scale of B from every rank's amax (one all_reduce
-MAX of two words) and computes its columns of C; an all_gather of C is timed separately, and the
-earlier mode (an independent seeded case per GPU, weak scaling) is reported beside it.  Timing is
+process per GPU): the same single GEMM per step, split into output tiles (strong scaling) -- the ranks
+form a pr x pc grid (1 x 2 for two GPUs, 2 x N/2 for four and eight), rank r holds its rows of A and of
+B, takes the global scales of the sharded operands from every rank's amax (one all_reduce MAX of two
+words) and computes its tile of C; an all_gather of C is timed separately, and the earlier mode (an
+independent seeded case per GPU, weak scaling) is reported beside it.  Timing is
 the max over ranks of CUDA-event time.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--mnk M,N,K]
@@ -459,23 +460,25 @@ def main() -> int:
 
     quant_fn, _real_fn, emul_fn, _meta = build_nvfp_fns(out_dtype=torch.bfloat16)
     stream = torch.cuda.current_stream(dev)
-    # one GEMM for the whole job: rank r holds all of A and rows [n0, n1) of B (output columns n0..n1)
-    n0, n1 = shard.column_range(N, world, rank)
-    a_h, b_full_h = make_inputs(0)
-    b_h = b_full_h[n0:n1].contiguous()
+    # one GEMM for the whole job: rank r holds rows [m0, m1) of A and rows [n0, n1) of B and computes the
+    # output tile C[m0:m1, n0:n1] (a pr x pc grid of ranks: shard.grid_shape)
+    pr, pc = shard.grid_shape(world)
+    (m0, m1), (n0, n1) = shard.tile_ranges(M, N, world, rank)
+    a_full_h, b_full_h = make_inputs(0)
+    a_h, b_h = a_full_h[m0:m1].contiguous(), b_full_h[n0:n1].contiguous()
     a_d, b_d = a_h.to(dev), b_h.to(dev)
 
     def step(a, b, ev=None):
         """quant_fn + emul_fn of this rank's share.  One GPU: the drop-in builders, unchanged.  Several:
-        the global scale of B from all ranks' amax (one all_reduce MAX of two words), then A and this
-        rank's B rows quantised and the emulated GEMM of C[:, n0:n1]."""
+        the global scales of the sharded operands from all ranks' amax (one all_reduce MAX of two words),
+        then this rank's rows of A and B quantised and the emulated GEMM of its tile C[m0:m1, n0:n1]."""
         if world == 1:
             st = quant_fn(a, b)
             if ev is not None:
                 ev[0].record(stream)
             out = emul_fn(st)
         else:
-            gsa, gsb, alpha = shard.sharded_global_scales(a, b, a_sharded=False, b_sharded=True)
+            gsa, gsb, alpha = shard.sharded_global_scales(a, b, a_sharded=pr > 1, b_sharded=pc > 1)
             (qa, sa), (qb, sb) = _lib.quant_nvfp4(a, gsa), _lib.quant_nvfp4(b, gsb)
             st = (qa, qb, sa, sb, alpha)
             if ev is not None:
@@ -513,11 +516,11 @@ def main() -> int:
     gather_ms = None
     if world > 1:
         g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        shard.gather_columns(out, N)
+        shard.gather_tiles(out, M, N)
         torch.cuda.synchronize()
         dist.barrier()
         g0.record(stream)
-        full = shard.gather_columns(out, N)
+        full = shard.gather_tiles(out, M, N)
         g1.record(stream)
         torch.cuda.synchronize()
         gather_ms = g0.elapsed_time(g1)
@@ -528,7 +531,7 @@ def main() -> int:
     # copies run on their own streams with two device input buffers, so step i's host->device copy
     # overlaps step i-1's compute and its device->host copy overlaps step i+1's (a serving pipeline).
     a_p, b_p = a_h.pin_memory(), b_h.pin_memory()
-    out_h = torch.empty((M, n1 - n0), dtype=torch.float16).pin_memory()
+    out_h = torch.empty((m1 - m0, n1 - n0), dtype=torch.float16).pin_memory()
     s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
     a_buf = [torch.empty_like(a_d), torch.empty_like(a_d)]
     b_buf = [torch.empty_like(b_d), torch.empty_like(b_d)]
@@ -604,7 +607,8 @@ def main() -> int:
 
     if rank == 0:
         macs = M * N * K                       # the whole job: one GEMM per step, split over the ranks
-        macs_rank = M * (n1 - n0) * K          # rank 0's share, for the per-launch roofline
+        mr, nr = m1 - m0, n1 - n0               # rank 0's tile, for the per-launch roofline
+        macs_rank = mr * nr * K
         value = macs * args.steps / (ms_max / 1e3)
         e2e_v = macs * args.steps / (e2e_max / 1e3)
         pk, pk_kind = peaks()
@@ -618,8 +622,7 @@ def main() -> int:
         fp64_ops = 2.0 * macs_rank / 64
         fp64_peak = 64.0 * n_sm * mhz * 1e6
         fp64_ms = fp64_ops / fp64_peak * 1e3
-        nr = n1 - n0
-        hbm_bytes = M * K // 2 + nr * K // 2 + (-(-M // 128) * 128 + -(-nr // 128) * 128) * (K // 16) + 2 * M * nr
+        hbm_bytes = mr * K // 2 + nr * K // 2 + (-(-mr // 128) * 128 + -(-nr // 128) * 128) * (K // 16) + 2 * mr * nr
         hbm_ms = hbm_bytes / (pk.get("hbm_gbs", 6650.0) * 1e9) * 1e3
         floors = {"tensor": tensor_ms, "fp64": fp64_ms, "hbm": hbm_ms}
         bound = max(floors, key=floors.get)    # the binding floor (FP64 at the benchmark shape)
@@ -644,10 +647,10 @@ def main() -> int:
                                    "columns x100, quant_fn + emul_fn per step, fp16 out",
                        "M": M, "N": N, "K": K, "format": "nvfp4", "w_reduce": 4, "rounding": "RZ/RZ",
                        "l2": "inputs larger than L2 (fp16 A+B = 268 MB read per step)",
-                       "parallelism": "one GEMM per step" + (f", output columns split over {world} GPUs (B rows "
-                                      f"{n1 - n0} per GPU, all of A on each), global scale of B by one "
-                                      "all_reduce MAX of amax words" if world > 1 else "")},
-            "e2e": {"value": e2e_v, "unit": "MAC/s", "h2d_bytes_per_step": world * (M * K * 2) + N * K * 2,
+                       "parallelism": "one GEMM per step" + (f", output tiles split over {world} GPUs as a {pr} x {pc} "
+                                      f"grid (A rows {m1 - m0}, B rows {n1 - n0} per GPU), global scales of the "
+                                      "sharded operands by one all_reduce MAX of amax words" if world > 1 else "")},
+            "e2e": {"value": e2e_v, "unit": "MAC/s", "h2d_bytes_per_step": pc * (M * K * 2) + pr * (N * K * 2),
                     "d2h_bytes_per_step": M * N * 2},
             "roofline": {"bound": bound, "achieved": achieved[bound], "peak": peak_of[bound],
                          "unit": "GB/s" if bound == "hbm" else "TFLOP/s",
@@ -655,7 +658,7 @@ def main() -> int:
                          "traffic": ncu_traffic() if (M, N, K) == (8192, 8192, 8192) and world == 1 else None,
                          "kernel": "one rank's emul_fn launches (pre-pass kernels + emul_gemm_tc_kernel), CUDA events",
                          "kernel_ms": gemm_max,
-                         "work_per_launch": f"M*n*K = {macs_rank} emulated MACs (n = this rank's columns): "
+                         "work_per_launch": f"m*n*K = {macs_rank} emulated MACs (m x n = this rank's tile): "
                                             f"{2 * macs_rank} stage-1 tensor flops, {fp64_ops:.4g} FP64 stage-4 "
                                             f"operations, {hbm_bytes} compulsory bytes",
                          "floors_ms": floors,
