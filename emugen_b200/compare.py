@@ -2,7 +2,9 @@
 
 Mirrors gemm_compare/runner.py:20-55 ``compare_tensors`` and 58-79 ``compare_mse`` (same arguments,
 same returned dicts).  The counting pass is one emu_compare kernel; only the per-mismatch samples of
-a failing comparison are gathered with torch indexing, on the device.
+a failing comparison are gathered with torch indexing, on the device.  ``gemm_compare_tensors`` gives
+the same dict for an emulated GEMM whose output is never written in full (the comparison fused into
+the GEMM's epilogue, emu_gemm_compare).
 """
 from __future__ import annotations
 
@@ -52,3 +54,36 @@ def compare_mse(reference: torch.Tensor, target: torch.Tensor) -> dict[str, Any]
         "per_gemm_rel_l2_error": (sq_sum ** 0.5) / max(ref_sq_sum ** 0.5, 1e-12),
         "mismatch_details": [],
     }
+
+
+def gemm_compare_tensors(a_fp4: torch.Tensor, b_fp4: torch.Tensor, scale_a: torch.Tensor, scale_b: torch.Tensor,
+                         real_output: torch.Tensor, *, fmt: int, group_size: int, w_reduce: int,
+                         stage3_rounding: int, stage4_rounding: int, alpha: torch.Tensor | None, out_mode: int,
+                         sample_count: int = 5) -> dict[str, Any]:
+    """``compare_tensors(real_output, emulated GEMM)`` without the emulated [M, N] output in memory: the
+    comparison runs in the GEMM's epilogue (emu_gemm_compare: mismatch count, max_diff and the row-major
+    index of the first mismatch).  When it finds mismatches, the mismatch samples are those of the
+    128-row blocks of A from the first mismatch's block on, recomputed one block at a time (the GEMM of
+    a row slice is bit for bit those rows of the whole GEMM) until ``sample_count`` are gathered -- the
+    first mismatches in row-major order, as the reference lists them (runner.py:38-49)."""
+    from .shard import ROW_BLOCK, row_slice
+
+    kw = dict(fmt=fmt, group_size=group_size, w_reduce=w_reduce, stage3_rounding=stage3_rounding,
+              stage4_rounding=stage4_rounding, alpha=alpha, out_mode=out_mode)
+    st, _ = _lib.gemm_compare(a_fp4, b_fp4, scale_a, scale_b, real_output, write_out=False, **kw)
+    max_diff = float(st["max_diff"])
+    status = "SUCCESS" if max_diff == 0 else "MISMATCH"
+    details: list[dict[str, Any]] = []
+    if status == "MISMATCH" and sample_count > 0:
+        M, N = a_fp4.shape[0], b_fp4.shape[0]
+        r0 = int(st["first_index"]) // N // ROW_BLOCK * ROW_BLOCK
+        while len(details) < sample_count and r0 < M:
+            r1 = min(M, r0 + ROW_BLOCK)
+            a_rows, sa_rows = row_slice(a_fp4, scale_a, r0, r1)
+            rows = _lib.gemm(a_rows, b_fp4, sa_rows, scale_b, **kw)
+            sub = compare_tensors(real_output[r0:r1], rows, sample_count=sample_count - len(details))
+            for d in sub["mismatch_details"]:
+                d["idx"] = (d["idx"][0] + r0, d["idx"][1])
+                details.append(d)
+            r0 = r1
+    return {"status": status, "max_diff": max_diff, "mismatch_details": details}

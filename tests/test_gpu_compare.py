@@ -214,3 +214,37 @@ def test_suite_on_device_emul_vs_emul():
               distributions=["normal", "student_t", "outliers"], seed=3)
     assert suite.run_suite(quant_fn, emul_fn, emul_fn, **kw) == 0
     assert suite.run_suite(quant_fn, lambda s: pseudo_fn(s).to(torch.float16), emul_fn, metric_mode="mse", **kw) == 0
+
+
+def test_fused_compare_returns_the_reference_mismatch_samples():
+    """compare.gemm_compare_tensors: the comparison fused into the tensor-core epilogue (no output
+    written) gives the same dict as compare_tensors on the full output -- status, max_diff and the
+    first mismatch samples in row-major order, gathered from recomputed 128-row blocks (here across
+    three blocks, with a NaN on the real side)."""
+    from emugen_b200 import _lib, compare, nvfp4_global_scales, quant_nvfp4
+
+    g = torch.Generator().manual_seed(31)
+    a = torch.randn(512, 1024, generator=g).half().cuda()
+    b = torch.randn(512, 1024, generator=g).half().cuda()
+    gsa, gsb, alpha = nvfp4_global_scales(a, b)
+    (qa, sa), (qb, sb) = quant_nvfp4(a, gsa), quant_nvfp4(b, gsb)
+    # 512 x 512 x 1024 (2^28 MACs) takes the tensor-core path, whose epilogue does the comparison
+    kw = dict(fmt=0, group_size=16, w_reduce=4, stage3_rounding=0, stage4_rounding=0, alpha=alpha, out_mode=0)
+    out = _lib.gemm(qa, qb, sa, sb, **kw)
+
+    def same(x, y):   # the two dicts equal, a NaN sample value equal to a NaN
+        def norm(d):
+            return [(e["idx"], "nan" if math.isnan(e["real"]) else e["real"], e["model"], e["diff"])
+                    for e in d["mismatch_details"]]
+        return x["status"] == y["status"] and x["max_diff"] == y["max_diff"] and norm(x) == norm(y)
+
+    assert same(compare.gemm_compare_tensors(qa, qb, sa, sb, out.clone(), **kw), compare.compare_tensors(out, out))
+    real = out.clone()
+    for r, c in ((130, 5), (130, 7), (131, 0), (300, 10), (511, 511)):
+        real[r, c] = real[r, c] + 1.0
+    real[300, 11] = float("nan")
+    for n in (1, 3, 5, 8):
+        got = compare.gemm_compare_tensors(qa, qb, sa, sb, real, sample_count=n, **kw)
+        assert same(got, compare.compare_tensors(real, out, sample_count=n))
+        assert [d["idx"] for d in got["mismatch_details"]] == [(130, 5), (130, 7), (131, 0), (300, 10), (300, 11),
+                                                               (511, 511)][:n]
