@@ -27,7 +27,7 @@ ABI_VERSION = 1
 SYMBOLS = ("emu_abi_version", "emu_last_error", "emu_status_string", "emu_gemm", "emu_gemm_workspace_size", "emu_gemm_tc_workspace_size",
            "emu_gemm_ws", "emu_gemm_tc_path_offset", "emu_gemm_static", "emu_nvfp4_global_scales", "emu_nvfp4_amax",
            "emu_nvfp4_scales_from_amax", "emu_quant_nvfp4", "emu_quant_mxfp4",
-           "emu_gemm_model", "emu_gemm_sweep", "emu_gemm_compare", "emu_compare", "emu_dequant_fp4", "emu_device_status",
+           "emu_gemm_model", "emu_gemm_sweep", "emu_gemm_compare", "emu_gemm_batch", "emu_compare", "emu_dequant_fp4", "emu_device_status",
            "emu_set_wait_limit", "emu_test_hold_first_ready")
 STATIC_SCRATCH_BYTES = 64 << 20   # EMU_STATIC_SCRATCH_BYTES
 
@@ -118,6 +118,9 @@ def load() -> ctypes.CDLL:
         L.emu_gemm_compare.restype = i32
         L.emu_gemm_compare.argtypes = [vp, vp, vp, vp, i64, i64, i64, i64, i64, i64, i64, vp,
                                        ctypes.POINTER(EmuGemmParams), vp, vp, vp, vp, ctypes.c_size_t, vp]
+        L.emu_gemm_batch.restype = i32
+        L.emu_gemm_batch.argtypes = [vp, vp, vp, vp, i64, i64, i64, i64, i64, i64, i64, vp,
+                                     ctypes.POINTER(EmuGemmParams), i32, vp, vp, vp, vp, ctypes.c_size_t, vp]
         L.emu_compare.restype = i32
         L.emu_compare.argtypes = [vp, vp, i32, i64, vp, vp]
         L.emu_dequant_fp4.restype = i32
@@ -414,6 +417,61 @@ def gemm_compare(a_fp4: torch.Tensor, b_fp4: torch.Tensor, scale_a: torch.Tensor
     device_status(dev)   # reading the statistics synchronises anyway
     host = EmuCompareStats.from_buffer_copy(bytes(st.cpu().numpy()))
     return {k: getattr(host, k) for k, _ in EmuCompareStats._fields_}, out
+
+
+def gemm_batch(a_fp4: torch.Tensor, b_fp4: torch.Tensor, scale_a: torch.Tensor, scale_b: torch.Tensor,
+               params, *, alpha: torch.Tensor | None = None, ref: torch.Tensor | None = None, write_out: bool = True,
+               path: str = "auto"):
+    """Several parameter sets on the same operands in one call (emu_gemm_batch).  `params`: a sequence of
+    (fmt, group_size, w_reduce, stage3_rounding, stage4_rounding, out_mode), every set with the first's
+    format, group size and out mode.  Returns (outputs [n, M, N] or None, a stats dict per set or None):
+    outputs when write_out, stats when `ref` is given (with write_out=False the comparisons run in the
+    tensor-core epilogue and no output is written)."""
+    L = load()
+    dev = _device_for(a_fp4, b_fp4, scale_a, scale_b)
+    M, N, K = a_fp4.shape[0], b_fp4.shape[0], a_fp4.shape[1] * 2
+    a = _bytes2d(a_fp4, dev, "a_fp4")
+    b = _bytes2d(b_fp4, dev, "b_fp4")
+    sa = _bytes2d(scale_a, dev, "scale_a")
+    sb = _bytes2d(scale_b, dev, "scale_b")
+    sets = [EmuGemmParams(*[int(x) for x in p]) for p in params]
+    n = len(sets)
+    arr = (EmuGemmParams * max(n, 1))(*sets)
+    odt = {EMU_OUT_F16: torch.float16, EMU_OUT_BF16_VIA_F16: torch.bfloat16, EMU_OUT_F32: torch.float32}[
+        sets[0].out_mode if n else EMU_OUT_F16]
+    r = None
+    if ref is not None:
+        r = ref.to(device=dev).contiguous()
+        if r.dtype != odt or tuple(r.shape) != (M, N):
+            raise RuntimeError(f"ref must be {odt} [{M}, {N}], got {r.dtype} {tuple(r.shape)}")
+    al = None if alpha is None else alpha.detach().reshape(1).to(device=dev, dtype=torch.float32).contiguous()
+    ws_ptr, ws_bytes, ws = None, 0, None
+    if path in ("auto", "tc") and n and M > 0 and N > 0 and K > 0:
+        query = L.emu_gemm_workspace_size if path == "auto" else L.emu_gemm_tc_workspace_size
+        need = query(M, N, K, ctypes.byref(sets[0]))
+        if need:
+            ws = torch.empty(need + 1024, dtype=torch.uint8, device=dev)
+            ws_ptr = (ws.data_ptr() + 1023) // 1024 * 1024
+            ws_bytes = need
+    out = torch.empty((n, M, N), dtype=odt, device=dev) if write_out else None
+    st = torch.empty(max(n, 1) * ctypes.sizeof(EmuCompareStats), dtype=torch.uint8, device=dev) if r is not None else None
+    with torch.cuda.device(dev):
+        status = L.emu_gemm_batch(a.data_ptr(), b.data_ptr(), sa.data_ptr(), sb.data_ptr(), M, N, K,
+                                  sa.shape[0], sa.shape[1], sb.shape[0], sb.shape[1],
+                                  None if al is None else al.data_ptr(), arr, n,
+                                  None if r is None else r.data_ptr(), None if out is None else out.data_ptr(),
+                                  None if st is None else st.data_ptr(), ws_ptr, ws_bytes, _stream(dev))
+    _check(status)
+    stats = None
+    if st is not None:
+        device_status(dev)
+        raw = bytes(st.cpu().numpy())
+        size = ctypes.sizeof(EmuCompareStats)
+        stats = []
+        for i in range(n):
+            h = EmuCompareStats.from_buffer_copy(raw[i * size:(i + 1) * size])
+            stats.append({k: getattr(h, k) for k, _ in EmuCompareStats._fields_})
+    return out, stats
 
 
 def gemm_model(a_fp4: torch.Tensor, b_fp4: torch.Tensor, scale_a: torch.Tensor, scale_b: torch.Tensor, *,

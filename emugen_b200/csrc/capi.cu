@@ -397,6 +397,35 @@ emu_status emu_gemm_compare(const uint8_t* a_fp4, const uint8_t* b_fp4, const ui
   return cuda_status(e, "emu_gemm_compare launch");
 }
 
+emu_status emu_gemm_batch(const uint8_t* a_fp4, const uint8_t* b_fp4, const uint8_t* scale_a,
+                          const uint8_t* scale_b, int64_t M, int64_t N, int64_t K, int64_t scale_a_rows,
+                          int64_t scale_a_cols, int64_t scale_b_rows, int64_t scale_b_cols, const float* alpha,
+                          const emu_gemm_params* params, int32_t n_params, const void* ref, void* out,
+                          emu_compare_stats* stats, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!params) return fail(EMU_ERR_INVALID_ARGUMENT, "params must not be NULL");
+  if (n_params < 1 || n_params > 4096) return fail(EMU_ERR_INVALID_ARGUMENT, "n_params must be in [1, 4096], got %d", n_params);
+  if (!out && !ref) return fail(EMU_ERR_INVALID_ARGUMENT, "out and ref are both NULL: nothing to produce");
+  if (ref && !stats) return fail(EMU_ERR_INVALID_ARGUMENT, "stats must not be NULL when ref is given");
+  for (int32_t i = 0; i < n_params; ++i) {
+    const emu_status st = validate_gemm(M, N, K, scale_a_rows, scale_a_cols, scale_b_rows, scale_b_cols, &params[i]);
+    if (st != EMU_OK) return st;
+    if (params[i].format != params[0].format || params[i].group_size != params[0].group_size ||
+        params[i].out_mode != params[0].out_mode)
+      return fail(EMU_ERR_INVALID_ARGUMENT, "params[%d]: every set must have params[0]'s format, group_size and out_mode", i);
+  }
+  const size_t elem = params[0].out_mode == EMU_OUT_F32 ? 4 : 2;
+  for (int32_t i = 0; i < n_params; ++i) {
+    void* oi = out ? static_cast<void*>(static_cast<char*>(out) + (size_t)i * (size_t)M * (size_t)N * elem) : nullptr;
+    const emu_status st =
+        ref ? emu_gemm_compare(a_fp4, b_fp4, scale_a, scale_b, M, N, K, scale_a_rows, scale_a_cols, scale_b_rows,
+                               scale_b_cols, alpha, &params[i], ref, oi, stats + i, workspace, workspace_bytes, stream)
+            : emu_gemm_ws(a_fp4, b_fp4, scale_a, scale_b, M, N, K, scale_a_rows, scale_a_cols, scale_b_rows,
+                          scale_b_cols, alpha, &params[i], oi, workspace, workspace_bytes, stream);
+    if (st != EMU_OK) return st;
+  }
+  return ok();
+}
+
 int64_t emu_set_wait_limit(int64_t cycles) { return emu::set_wait_limit(cycles); }
 
 emu_status emu_test_hold_first_ready(int32_t enable) {

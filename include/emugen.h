@@ -343,6 +343,25 @@ EMU_API emu_status emu_gemm_compare(const uint8_t* a_fp4, const uint8_t* b_fp4, 
                                     size_t workspace_bytes, void* stream);
 
 /*
+ * Several parameter sets on the same operands in one call: for i in [0, n_params), the emulated GEMM of
+ * emu_gemm_ws under params[i], written to out + i * M * N elements (all sets' outputs back to back,
+ * [n_params][M][N]) when `out` is not NULL, and compared with `ref` ([M][N]) into stats[i] as
+ * emu_gemm_compare does when `ref` is not NULL (then `stats` points to n_params structs; with no `out`
+ * the comparison runs in the tensor-core epilogue, which needs the workspace and a shape that path
+ * takes).  The operands fix the format and group size, and `out` / `ref` one element type, so every
+ * set has params[0]'s format, group_size and out_mode; block size and roundings vary per set.  The
+ * workspace is sized as for emu_gemm_ws (the size does not depend on the block size or roundings).
+ * The batched entry the survey of the reference's callers asks for (one call per sweep of rounding /
+ * block-size settings instead of one per setting); no counterpart in the reference, which runs one
+ * emulation per call.  n_params <= 4096.
+ */
+EMU_API emu_status emu_gemm_batch(const uint8_t* a_fp4, const uint8_t* b_fp4, const uint8_t* scale_a,
+                                  const uint8_t* scale_b, int64_t M, int64_t N, int64_t K, int64_t scale_a_rows,
+                                  int64_t scale_a_cols, int64_t scale_b_rows, int64_t scale_b_cols, const float* alpha,
+                                  const emu_gemm_params* params, int32_t n_params, const void* ref, void* out,
+                                  emu_compare_stats* stats, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
  * Dequantise packed FP4 to f32: out[r][k] = e2m1(q[r][k]) * scale(r, k / group), scales in the
  * swizzled layout ([pad128(rows)][sf_cols]).  MXFP4: scale = f32 with bits (u << 23) (u = 0 -> 0,
  * u = 255 -> inf), as flashinfer.mxfp4_dequantize, the reference's MXFP4 pseudo_fn operand

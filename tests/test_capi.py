@@ -89,3 +89,35 @@ def test_wait_limit_and_status_names():
         L.emu_set_wait_limit(prev)
     assert L.emu_status_string(_lib.EMU_ERR_TIMEOUT) == b"EMU_ERR_TIMEOUT"
     assert L.emu_test_hold_first_ready(0) == _lib.EMU_OK
+
+
+def _batch_status(sets, n=None, out=True, ref=False, stats=True, M=4, N=4, K=64):
+    L = _lib.load()
+    arr = (_lib.EmuGemmParams * max(len(sets), 1))(*[_lib.EmuGemmParams(*s) for s in sets]) if sets else None
+    fake = ctypes.c_void_p(256)  # never dereferenced: validation fails before any device access
+    st = L.emu_gemm_batch(fake, fake, fake, fake, M, N, K, 128, 4, 128, 4, None, arr,
+                          len(sets) if n is None else n, fake if ref else None, fake if out else None,
+                          fake if stats else None, None, 0, None)
+    return st, L.emu_last_error().decode()
+
+
+NV = (0, 16, 4, 0, 0, 0)
+
+
+@pytest.mark.parametrize("kw,msg", [
+    (dict(sets=[]), "params must not be NULL"),
+    (dict(sets=[NV], n=0), "n_params must be in [1, 4096]"),
+    (dict(sets=[NV], n=5000), "n_params must be in [1, 4096]"),
+    (dict(sets=[NV], out=False), "out and ref are both NULL"),
+    (dict(sets=[NV], ref=True, stats=False), "stats must not be NULL"),
+    (dict(sets=[NV, (1, 32, 2, 0, 0, 0)]), "params[1]: every set must have params[0]'s format"),
+    (dict(sets=[NV, (0, 16, 4, 0, 0, 2)]), "params[1]: every set must have params[0]'s format"),
+])
+def test_gemm_batch_validation(kw, msg):
+    st, err = _batch_status(**kw)
+    assert st == 1 and msg in err
+
+
+def test_gemm_batch_checks_every_set_like_emu_gemm():
+    st, err = _batch_status([NV, (0, 16, 0, 0, 0, 0)])
+    assert st == 8 and "w_reduce must be in [1, 64]" in err
