@@ -21,6 +21,9 @@ CASES = [
     ("nvfp", "fp16_round", 16, 8192, 512, 4, 1, 1, 2),       # stage-1 rounding (flagged groups)
     ("nvfp", "cancel", 9, 8256, 1024, 1, 0, 0, 2),           # block size read at run time
     ("nvfp", "huge_scales", 33, 8192, 640, 8, 0, 0, 0),      # three 16-row passes
+    # blocks of 64 / 32 groups of the largest E4M3 scales: the int64 block sums take the int64 -> f64
+    # conversion (exact below 2^53, i.e. up to 64 groups), not the 1.5 * 2^52 bias of blocks up to 16
+    ("nvfp", "huge_scales", 8, 8192, 2048, 64, 1, 0, 2),
     ("nvfp", "tiny_scales", 127, 8192, 256, 16, 1, 0, 2),    # one block: R3
     ("nvfp", "abs_normal", 24, 9000, 64, 4, 0, 1, 0),        # K = one block
     ("mxfp", "normal", 8, 8192, 4096, 2, 0, 0, 1),
@@ -34,6 +37,7 @@ CASES = [
     ("nvfp", "raw_nan_scales", 1, 32768, 9216, 4, 1, 1, 1),  # three windows; NaN scale codes in A and B
     ("nvfp", "fp16_round", 1, 32768, 4160, 1, 0, 1, 2),      # flagged groups; a 64-element last window
     ("nvfp", "huge_scales", 1, 33000, 5120, 16, 1, 0, 0),    # block size 16 (run time)
+    ("nvfp", "huge_scales", 1, 32768, 4096, 32, 0, 1, 2),    # block size 32: int64 -> f64 conversion
     ("mxfp", "raw_scales_full", 1, 32768, 8256, 2, 0, 1, 2), # UE8M0 0 and 255 (inf)
     ("mxfp", "subnormal_acc", 1, 32900, 2048, 1, 1, 1, 0),
     ("mxfp", "normal", 1, 32768, 1024, 2, 0, 0, 1),
